@@ -1,0 +1,113 @@
+/*
+ * nvfp4_b200.h - C ABI of the B200-native NVFP4 block-scaled GEMM library.
+ *
+ * Data formats (identical to the reference's input tuples):
+ *   a, b      : e2m1 codes, two per byte (element 2i in the low nibble),
+ *               K-major; a is (L, M, K/2) bytes, b is (L, N, K/2) bytes.
+ *               (kernels/gemm/reference.py:86-93, task.py:4)
+ *   sf*_perm  : e4m3 scale factors, one per 16 elements along K, in the
+ *               pre-permuted 128x4 "blocked" layout: storage order
+ *               (L, ceil(MN/128), ceil(K/64), 32, 4, 4) bytes; row r, K-vector j
+ *               of one 128-row block sits at byte (r%32)*16 + (r/32)*4 + j%4 of
+ *               atom (j/4).  (kernels/gemm/reference.py:113-150)
+ *   c         : fp16, (L, M, N) row-major, written in place (no beta).
+ * Computation: C = fp16( sum_k e2m1(A)*sfA * e2m1(B)*sfB ), fp32 accumulation.
+ *
+ * Every entry point launches on the given CUDA stream (cudaStream_t passed
+ * as void*, NULL = legacy default stream) and never synchronises it.  Return
+ * value 0 = launched; otherwise an NVFP4_ERR_* code, with a message from
+ * nvfp4_last_error().  Device-side failures (a pipeline wait that ran out)
+ * are recorded in a per-device status word: see nvfp4_status_get().
+ */
+#ifndef NVFP4_B200_H
+#define NVFP4_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NVFP4_ABI_VERSION 1
+
+#define NVFP4_OK 0
+#define NVFP4_ERR_INVALID_ARG 1   /* null pointer, non-positive size, bad group table */
+#define NVFP4_ERR_ALIGNMENT 2     /* a/b/scales not 16-byte aligned, c not 2-byte aligned */
+#define NVFP4_ERR_UNSUPPORTED 3   /* k not a multiple of 64, wrong GPU, too many groups */
+#define NVFP4_ERR_CUDA 4          /* a CUDA runtime call failed */
+#define NVFP4_ERR_DRIVER 5        /* tensor-map encoding through the driver failed */
+#define NVFP4_ERR_WORKSPACE 6     /* workspace missing or too small */
+
+/* Device status word values (nvfp4_status_get). */
+#define NVFP4_STATUS_OK 0
+#define NVFP4_STATUS_TIMEOUT_PRODUCER 1
+#define NVFP4_STATUS_TIMEOUT_MMA 2
+#define NVFP4_STATUS_TIMEOUT_EPILOGUE 3
+#define NVFP4_STATUS_TIMEOUT_DRAIN 4
+#define NVFP4_STATUS_BAD_GROUP 5
+
+/* Tuning / test knobs; zero-initialise and set what you need. */
+typedef struct nvfp4_options {
+  int operand_order;              /* 0 = auto; 1 = A feeds the 128-row MMA side;
+                                     2 = B feeds it ("swap", for skinny M) */
+  int tile_n;                     /* 0 = auto; else 32, 64, 128, 192 or 256 */
+  int max_ctas;                   /* 0 = one CTA per SM */
+  unsigned long long timeout_ns;  /* 0 = library default (2 s per pipeline wait) */
+  int debug_skip_producer;        /* test hook: issue no loads so every wait runs out */
+} nvfp4_options;
+
+/* Human-readable message for the last error returned on this thread. */
+const char* nvfp4_last_error(void);
+int nvfp4_abi_version(void);
+
+/* Per-wait timeout used by kernels launched afterwards (0 restores 2 s). */
+int nvfp4_set_timeout_ns(unsigned long long ns);
+
+/* Synchronous read / reset of the current device's status word. */
+int nvfp4_status_get(int* out);
+int nvfp4_status_reset(void);
+
+/*
+ * Dense NVFP4 GEMM, C[l] = A[l] * B[l]^T.
+ * Replaces custom_kernel() of kernels/gemm/submission.py:772-794 (which reads
+ * a, b, sfa_permuted, sfb_permuted, c and writes c in place) and its launch
+ * path my_kernel(), kernels/gemm/submission.py:586-746.
+ * Requirements: m, n, l >= 1; k >= 64 and k % 64 == 0.
+ */
+int nvfp4_gemm(const void* a, const void* b, const void* sfa_perm, const void* sfb_perm, void* c,
+               int m, int n, int k, int l, void* stream);
+
+/* Same as nvfp4_gemm with tuning / test options (opt may be NULL). */
+int nvfp4_gemm_ex(const void* a, const void* b, const void* sfa_perm, const void* sfb_perm, void* c,
+                  int m, int n, int k, int l, void* stream, const nvfp4_options* opt);
+
+/*
+ * Grouped NVFP4 GEMM: for every group g, C_g = A_g * B_g^T (l must be 1).
+ * Replaces custom_kernel() of kernels/group_gemm/submission.py:962-1087 and its
+ * device tables (problem sizes G x 4 int32, a/b/c pointers G x 3 int64,
+ * sfa/sfb permuted-scale pointers G x 2 int64: submission.py:993-1013).
+ * All three tables are DEVICE pointers, so a router kernel can fill them
+ * without a host round trip; groups with m == 0 or n == 0 are skipped.
+ * workspace: device memory of nvfp4_grouped_gemm_workspace_size(G) bytes,
+ * 256-byte aligned, not shared with a call in flight on another stream.
+ * Requirements per group: k % 64 == 0, k >= 64, a/b/sf 16-byte aligned.
+ * A group that violates them is skipped and NVFP4_STATUS_BAD_GROUP is
+ * recorded in the status word.  1 <= G <= 1024.
+ */
+size_t nvfp4_grouped_gemm_workspace_size(int G);
+
+int nvfp4_grouped_gemm(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev,
+                       const uint64_t* sf_ptrs_dev, int G, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* Same with tuning / test options (tile_n = 64, 128 or 256 token rows per tile). */
+int nvfp4_grouped_gemm_ex(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev,
+                          const uint64_t* sf_ptrs_dev, int G, void* workspace,
+                          size_t workspace_bytes, void* stream, const nvfp4_options* opt);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVFP4_B200_H */

@@ -1,0 +1,436 @@
+// C-ABI of the NVFP4 B200 library (declared in include/nvfp4_b200.h).
+//
+// Host responsibilities: argument checks, TMA tensor-map encoding (through the
+// driver entry point, so the library does not link libcuda), tile-shape
+// dispatch, and the launch on the caller's stream.  Nothing here synchronises
+// the stream; device-side errors (timed-out waits) land in a status word that
+// nvfp4_status_get() reads.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "nvfp4_kernels.cuh"
+#include "../../include/nvfp4_b200.h"
+
+using namespace nvfp4;
+
+// ------------------------------------------------------------------ status word
+// One word per device that loads the library; kernels record the first error here.
+__device__ int g_nvfp4_status;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;  // 2 s per wait
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(NVFP4_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+struct DeviceState {
+  bool init = false;
+  int num_sms = 0;
+  int* status = nullptr;  // device address of g_nvfp4_status
+};
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+unsigned long long g_timeout_ns = kDefaultTimeoutNs;
+
+int device_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_CUDA, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& st = g_dev[dev];
+  if (!st.init) {
+    e = cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0)
+      return fail(NVFP4_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only",
+                  dev, major, minor);
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.status), g_nvfp4_status);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    if (!g_encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return fail(NVFP4_ERR_DRIVER, "cuTensorMapEncodeTiled entry point not available");
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    st.init = true;
+  }
+  *out = &st;
+  return NVFP4_OK;
+}
+
+// Operand map: a (rows x kbytes x batch) uint8 tensor, K-major, 128-byte swizzle,
+// box = 128 bytes of K x box_rows rows.  Out-of-range rows read as zero.
+int encode_operand_map(CUtensorMap* m, const void* ptr, long long rows, long long kbytes,
+                       long long batch, int box_rows) {
+  cuuint64_t dims[3] = {(cuuint64_t)kbytes, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)kbytes, (cuuint64_t)(rows * kbytes)};
+  cuuint32_t box[3] = {128u, (cuuint32_t)box_rows, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), dims, strides,
+                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(NVFP4_ERR_DRIVER, "cuTensorMapEncodeTiled failed (%d) rows=%lld kbytes=%lld", (int)r,
+                rows, kbytes);
+  return NVFP4_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <bool GROUPED, bool SWAP, int BN>
+int launch(const CUtensorMap& tp, const CUtensorMap& tq, const GemmParams& prm, int grid,
+           cudaStream_t stream) {
+  using C_ = Cfg<BN>;
+  auto kern = nvfp4_gemm_kernel<GROUPED, SWAP, BN>;
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    attr_done[dev] = true;
+  }
+  kern<<<grid, kNumThreads, C_::kSmemBytes, stream>>>(tp, tq, prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "nvfp4_gemm_kernel launch");
+  return NVFP4_OK;
+}
+
+struct DenseChoice {
+  bool swap;
+  int bn;
+};
+
+DenseChoice choose_dense(int m, int n, int k, const nvfp4_options* opt) {
+  (void)k;
+  DenseChoice c;
+  if (m <= 64) c = {true, 64};
+  else if (m <= 128) c = {true, 128};
+  else c = {false, (n >= 2048) ? 256 : 128};
+  if (opt) {
+    if (opt->operand_order == 1) c.swap = false;
+    if (opt->operand_order == 2) c.swap = true;
+    if (opt->tile_n > 0) c.bn = opt->tile_n;
+  }
+  return c;
+}
+
+template <bool SWAP, int BN>
+int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb, void* c, int m,
+                 int n, int k, int l, cudaStream_t stream, DeviceState* st,
+                 const nvfp4_options* opt) {
+  // P feeds the 128-row MMA side, Q the BN side.
+  const void* P = SWAP ? b : a;
+  const void* Q = SWAP ? a : b;
+  const void* sfP = SWAP ? sfb : sfa;
+  const void* sfQ = SWAP ? sfa : sfb;
+  const int p_rows = SWAP ? n : m;
+  const int q_rows = SWAP ? m : n;
+  const long long kbytes = k / 2;
+  CUtensorMap tp, tq;
+  int rc = encode_operand_map(&tp, P, p_rows, kbytes, l, kBM);
+  if (rc) return rc;
+  rc = encode_operand_map(&tq, Q, q_rows, kbytes, l, BN);
+  if (rc) return rc;
+  GemmParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.p_rows = p_rows;
+  prm.q_rows = q_rows;
+  prm.K = k;
+  prm.L = l;
+  const long long rk = (k + 63) / 64;
+  prm.sf_p = static_cast<const uint8_t*>(sfP);
+  prm.sf_q = static_cast<const uint8_t*>(sfQ);
+  prm.sf_p_batch = (long long)((p_rows + 127) / 128) * rk * kAtomBytes;
+  prm.sf_q_batch = (long long)((q_rows + 127) / 128) * rk * kAtomBytes;
+  prm.C = static_cast<__half*>(c);
+  prm.ldc = n;
+  prm.c_batch = (long long)m * n;
+  prm.tiles_p = (p_rows + kBM - 1) / kBM;
+  prm.tiles_q = (q_rows + BN - 1) / BN;
+  const long long total = (long long)prm.tiles_p * prm.tiles_q * l;
+  if (total > 0x7fffffffLL) return fail(NVFP4_ERR_UNSUPPORTED, "too many tiles");
+  prm.total_tiles = (int)total;
+  prm.q_fastest = 0;
+  prm.status = st->status;
+  prm.timeout_ns = (opt && opt->timeout_ns) ? opt->timeout_ns : g_timeout_ns;
+  prm.debug_skip_producer = opt ? opt->debug_skip_producer : 0;
+  int grid = st->num_sms;
+  if (opt && opt->max_ctas > 0 && opt->max_ctas < grid) grid = opt->max_ctas;
+  if (grid > prm.total_tiles) grid = prm.total_tiles;
+  return launch<false, SWAP, BN>(tp, tq, prm, grid, stream);
+}
+
+// ------------------------------------------------------------------ grouped GEMM
+constexpr int kMaxGroups = 1024;
+constexpr int kGroupedBN = 128;  // token rows per tile (MMA N side)
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+size_t grouped_ws_bytes(int G) {
+  return align_up((size_t)G * 2 * sizeof(CUtensorMap), 256) + align_up((size_t)(G + 1) * 4, 256);
+}
+
+__device__ __forceinline__ void tmap_replace_addr(void* m, const void* p) {
+  asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "l"(reinterpret_cast<uint64_t>(p))
+               : "memory");
+}
+template <int ORD>
+__device__ __forceinline__ void tmap_replace_dim(void* m, uint32_t v) {
+  asm volatile("tensormap.replace.tile.global_dim.global.b1024.b32 [%0], %1, %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "n"(ORD), "r"(v)
+               : "memory");
+}
+template <int ORD>
+__device__ __forceinline__ void tmap_replace_stride(void* m, uint64_t v) {
+  asm volatile("tensormap.replace.tile.global_stride.global.b1024.b64 [%0], %1, %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "n"(ORD), "l"(v)
+               : "memory");
+}
+
+// One thread per group: validate the group, clone the two template maps into
+// the workspace and point them at the group's B (P side) and A (Q side), then
+// a block-wide scan turns per-group tile counts into the schedule prefix.
+__global__ void __launch_bounds__(kMaxGroups)
+nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_constant__ CUtensorMap tmpl_q,
+                   const int* __restrict__ sizes, const unsigned long long* __restrict__ abc,
+                   const unsigned long long* __restrict__ sfs, int G, CUtensorMap* maps,
+                   int* prefix, int bn, int* status) {
+  __shared__ int warp_sums[kMaxGroups / 32];
+  const int g = threadIdx.x;
+  int tiles = 0;
+  if (g < G) {
+    const int m = sizes[4 * g + 0], n = sizes[4 * g + 1], k = sizes[4 * g + 2], l = sizes[4 * g + 3];
+    const unsigned long long pa = abc[3 * g + 0], pb = abc[3 * g + 1], pc = abc[3 * g + 2];
+    const unsigned long long sa = sfs[2 * g + 0], sb = sfs[2 * g + 1];
+    const bool empty = (m == 0 || n == 0);
+    const bool valid = m >= 0 && n >= 0 && l == 1 && k >= 64 && (k % 64) == 0 &&
+                       ((pa | pb | sa | sb) & 15ull) == 0 && (pc & 1ull) == 0 &&
+                       (empty || (pa && pb && pc && sa && sb));
+    if (!valid) {
+      atomicCAS(status, 0, 5 /* NVFP4_STATUS_BAD_GROUP */);
+    } else if (!empty) {
+      tiles = ((n + kBM - 1) / kBM) * ((m + bn - 1) / bn);
+      CUtensorMap* mp = maps + 2 * g;
+      CUtensorMap* mq = maps + 2 * g + 1;
+      *mp = tmpl_p;
+      *mq = tmpl_q;
+      const uint64_t kbytes = (uint64_t)k / 2;
+      tmap_replace_addr(mp, reinterpret_cast<const void*>(pb));
+      tmap_replace_dim<0>(mp, (uint32_t)kbytes);
+      tmap_replace_dim<1>(mp, (uint32_t)n);
+      tmap_replace_stride<0>(mp, kbytes);
+      tmap_replace_stride<1>(mp, kbytes * (uint64_t)n);
+      tmap_replace_addr(mq, reinterpret_cast<const void*>(pa));
+      tmap_replace_dim<0>(mq, (uint32_t)kbytes);
+      tmap_replace_dim<1>(mq, (uint32_t)m);
+      tmap_replace_stride<0>(mq, kbytes);
+      tmap_replace_stride<1>(mq, kbytes * (uint64_t)m);
+      asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
+    }
+  }
+  // inclusive block scan of tile counts
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int v = tiles;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += u;
+  }
+  if (lane == 31) warp_sums[wid] = v;
+  __syncthreads();
+  if (wid == 0) {
+    const int nw = blockDim.x / 32;
+    int w = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += u;
+    }
+    if (lane < nw) warp_sums[lane] = w;
+  }
+  __syncthreads();
+  const int incl = v + (wid > 0 ? warp_sums[wid - 1] : 0);
+  if (g < G) prefix[g + 1] = incl;
+  if (g == 0) prefix[0] = 0;
+}
+
+template <int BN>
+int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sfs, int G, void* ws,
+                   cudaStream_t stream, DeviceState* st, const nvfp4_options* opt) {
+  // Templates: any valid 16-byte-aligned address and sizes; the prep kernel
+  // replaces address, extents and strides per group.
+  CUtensorMap tp, tq;
+  int rc = encode_operand_map(&tp, ws, 128, 128, 1, kBM);
+  if (rc) return rc;
+  rc = encode_operand_map(&tq, ws, 128, 128, 1, BN);
+  if (rc) return rc;
+  CUtensorMap* maps = static_cast<CUtensorMap*>(ws);
+  int* prefix = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) +
+                                       align_up((size_t)G * 2 * sizeof(CUtensorMap), 256));
+  const int threads = ((G + 31) / 32) * 32;
+  nvfp4_grouped_prep<<<1, threads, 0, stream>>>(tp, tq, sizes,
+                                                reinterpret_cast<const unsigned long long*>(abc),
+                                                reinterpret_cast<const unsigned long long*>(sfs), G,
+                                                maps, prefix, BN, st->status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "nvfp4_grouped_prep launch");
+  GemmParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.G = G;
+  prm.sizes = sizes;
+  prm.abc = reinterpret_cast<const unsigned long long*>(abc);
+  prm.sfs = reinterpret_cast<const unsigned long long*>(sfs);
+  prm.maps = maps;
+  prm.tile_prefix = prefix;
+  prm.status = st->status;
+  prm.timeout_ns = (opt && opt->timeout_ns) ? opt->timeout_ns : g_timeout_ns;
+  prm.debug_skip_producer = opt ? opt->debug_skip_producer : 0;
+  int grid = st->num_sms;
+  if (opt && opt->max_ctas > 0 && opt->max_ctas < grid) grid = opt->max_ctas;
+  return launch<true, true, BN>(tp, tq, prm, grid, stream);
+}
+
+}  // namespace
+
+// ======================================================================= C ABI
+extern "C" {
+
+const char* nvfp4_last_error(void) { return g_last_error.c_str(); }
+
+int nvfp4_abi_version(void) { return NVFP4_ABI_VERSION; }
+
+int nvfp4_set_timeout_ns(unsigned long long ns) {
+  g_timeout_ns = ns ? ns : kDefaultTimeoutNs;
+  return NVFP4_OK;
+}
+
+int nvfp4_status_get(int* out) {
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_nvfp4_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(status)");
+  if (out) *out = v;
+  return NVFP4_OK;
+}
+
+int nvfp4_status_reset(void) {
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  int zero = 0;
+  cudaError_t e = cudaMemcpyToSymbol(g_nvfp4_status, &zero, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(status)");
+  return NVFP4_OK;
+}
+
+int nvfp4_gemm_ex(const void* a, const void* b, const void* sfa_perm, const void* sfb_perm, void* c,
+                  int m, int n, int k, int l, void* stream, const nvfp4_options* opt) {
+  if (!a || !b || !sfa_perm || !sfb_perm || !c)
+    return fail(NVFP4_ERR_INVALID_ARG, "null pointer argument");
+  if (m <= 0 || n <= 0 || k <= 0 || l <= 0)
+    return fail(NVFP4_ERR_INVALID_ARG, "m, n, k, l must be positive (got %d, %d, %d, %d)", m, n, k, l);
+  if (k % 64 != 0)
+    return fail(NVFP4_ERR_UNSUPPORTED, "k must be a multiple of 64 (got %d)", k);
+  if (!aligned16(a) || !aligned16(b) || !aligned16(sfa_perm) || !aligned16(sfb_perm))
+    return fail(NVFP4_ERR_ALIGNMENT, "a, b and the scale tensors must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(c) & 1u) != 0)
+    return fail(NVFP4_ERR_ALIGNMENT, "c must be 2-byte aligned");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DenseChoice ch = choose_dense(m, n, k, opt);
+#define NVFP4_DENSE_CASE(SW, BNV)                                                         \
+  if (ch.swap == SW && ch.bn == BNV)                                                      \
+    return run_dense_bn<SW, BNV>(a, b, sfa_perm, sfb_perm, c, m, n, k, l, s, st, opt);
+  NVFP4_DENSE_CASE(true, 64)
+  NVFP4_DENSE_CASE(true, 128)
+  NVFP4_DENSE_CASE(true, 256)
+  NVFP4_DENSE_CASE(false, 64)
+  NVFP4_DENSE_CASE(false, 128)
+  NVFP4_DENSE_CASE(false, 192)
+  NVFP4_DENSE_CASE(false, 256)
+#undef NVFP4_DENSE_CASE
+  return fail(NVFP4_ERR_UNSUPPORTED, "no kernel for swap=%d tile_n=%d", (int)ch.swap, ch.bn);
+}
+
+int nvfp4_gemm(const void* a, const void* b, const void* sfa_perm, const void* sfb_perm, void* c,
+               int m, int n, int k, int l, void* stream) {
+  return nvfp4_gemm_ex(a, b, sfa_perm, sfb_perm, c, m, n, k, l, stream, nullptr);
+}
+
+size_t nvfp4_grouped_gemm_workspace_size(int G) {
+  if (G <= 0 || G > kMaxGroups) return 0;
+  return grouped_ws_bytes(G);
+}
+
+int nvfp4_grouped_gemm_ex(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev,
+                          const uint64_t* sf_ptrs_dev, int G, void* workspace,
+                          size_t workspace_bytes, void* stream, const nvfp4_options* opt) {
+  if (G <= 0 || G > kMaxGroups)
+    return fail(NVFP4_ERR_UNSUPPORTED, "group count %d outside [1, %d]", G, kMaxGroups);
+  if (!sizes_dev || !abc_ptrs_dev || !sf_ptrs_dev)
+    return fail(NVFP4_ERR_INVALID_ARG, "null group table");
+  if (!workspace || workspace_bytes < grouped_ws_bytes(G))
+    return fail(NVFP4_ERR_WORKSPACE, "workspace needs %zu bytes", grouped_ws_bytes(G));
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(NVFP4_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int bn = (opt && opt->tile_n > 0) ? opt->tile_n : kGroupedBN;
+  switch (bn) {
+    case 64: return run_grouped_bn<64>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
+    case 128: return run_grouped_bn<128>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
+    case 256: return run_grouped_bn<256>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
+    default: return fail(NVFP4_ERR_UNSUPPORTED, "grouped tile_n %d not built", bn);
+  }
+}
+
+int nvfp4_grouped_gemm(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev,
+                       const uint64_t* sf_ptrs_dev, int G, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  return nvfp4_grouped_gemm_ex(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, workspace_bytes,
+                               stream, nullptr);
+}
+
+}  // extern "C"

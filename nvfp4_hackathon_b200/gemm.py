@@ -1,0 +1,71 @@
+"""Drop-in for the reference's dense NVFP4 GEMM entry points
+(kernels/gemm/submission.py:752 ``compile_kernel`` and :772 ``custom_kernel``).
+
+``custom_kernel(data)`` takes the reference's 7-tuple, reads a, b and the two
+permuted scale tensors, writes c in place on the current CUDA stream and
+returns c, like the reference (submission.py:774-794).  The plain scale
+tensors are ignored, as in the reference.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native
+from .layout import SF_VEC, ceil_div, is_permuted_layout
+from .task import gemm_input_t, gemm_output_t
+
+_compiled = None
+
+
+def compile_kernel():
+    """Load the precompiled sm_100a library (the reference JIT-compiles here,
+    submission.py:752-769).  Returns the callable entry point."""
+    global _compiled
+    if _compiled is None:
+        _native.load()
+        _compiled = custom_kernel
+    return _compiled
+
+
+def _check_operand(t: torch.Tensor, rows: int, kb: int, l: int, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if tuple(t.shape) != (rows, kb, l):
+        raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {(rows, kb, l)}")
+    want = (kb, 1, rows * kb)
+    if any(sz > 1 and st != w for sz, st, w in zip(t.shape, t.stride(), want)):
+        raise ValueError(f"{name} must be K-major with batch outermost, strides {want}; got {t.stride()}")
+
+
+def launch(a, b, sfa_perm, sfb_perm, c, m: int, n: int, k: int, l: int, stream=None,
+           opt: _native.Nvfp4Options | None = None) -> None:
+    """Raw launch on device pointers (tensors or ints); no layout checks."""
+    lib = _native.load()
+    ptr = lambda x: x if isinstance(x, int) else x.data_ptr()
+    s = torch.cuda.current_stream().cuda_stream if stream is None else stream
+    if opt is None:
+        rc = lib.nvfp4_gemm(ptr(a), ptr(b), ptr(sfa_perm), ptr(sfb_perm), ptr(c), m, n, k, l, s)
+    else:
+        rc = lib.nvfp4_gemm_ex(ptr(a), ptr(b), ptr(sfa_perm), ptr(sfb_perm), ptr(c), m, n, k, l, s,
+                               ctypes.byref(opt))
+    _native.check(rc, "nvfp4_gemm")
+
+
+def custom_kernel(data: gemm_input_t, opt: _native.Nvfp4Options | None = None) -> gemm_output_t:
+    a, b, _, _, sfa_perm, sfb_perm, c = data
+    m, kb, l = a.shape
+    n = b.shape[0]
+    k = 2 * kb  # two e2m1 values per byte (submission.py:779)
+    _check_operand(a, m, kb, l, "a")
+    _check_operand(b, n, kb, l, "b")
+    if c.dtype != torch.float16 or tuple(c.shape) != (m, n, l):
+        raise ValueError(f"c must be float16 of shape {(m, n, l)}")
+    if any(sz > 1 and st != w for sz, st, w in zip(c.shape, c.stride(), (n, 1, m * n))):
+        raise ValueError(f"c must have strides {(n, 1, m * n)}; got {c.stride()}")
+    sf_k = ceil_div(k, SF_VEC)
+    if not is_permuted_layout(sfa_perm, m, sf_k, l) or not is_permuted_layout(sfb_perm, n, sf_k, l):
+        raise ValueError("scale tensors must use the permuted (32, 4, rest_mn, 4, rest_k, l) layout")
+    launch(a, b, sfa_perm, sfb_perm, c, m, n, k, l, opt=opt)
+    return c

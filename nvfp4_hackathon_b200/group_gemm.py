@@ -1,0 +1,104 @@
+"""Drop-in for the reference's grouped NVFP4 GEMM entry points
+(kernels/group_gemm/submission.py:913 ``compile_kernel(problem_sizes)`` and
+:962 ``custom_kernel(data)``).
+
+The host packs the per-group sizes and pointers into one device table (as the
+reference does every call, submission.py:993-1013), but caches it keyed on
+the pointers and sizes, so a repeated call with the same tensors issues no
+host-to-device copy.  The kernel schedule is built on the device from that
+table, so there is no compile-time tile list to go stale (the reference keys
+its compiled tile list on the group count only, submission.py:924).
+"""
+from __future__ import annotations
+
+import ctypes
+from collections import OrderedDict
+
+import torch
+
+from . import _native
+from .layout import SF_VEC, ceil_div, is_permuted_layout
+from .task import group_input_t, group_output_t
+
+_TABLE_CACHE: "OrderedDict[tuple, torch.Tensor]" = OrderedDict()
+_TABLE_CACHE_MAX = 64
+_WORKSPACES: dict[tuple, torch.Tensor] = {}
+
+
+def compile_kernel(problem_sizes=None):
+    """Load the precompiled library; ``problem_sizes`` is accepted for API parity."""
+    _native.load()
+    return custom_kernel
+
+
+def _table(abc, sfp, sizes, device) -> torch.Tensor:
+    """Device int64 buffer: [sizes (G x 4 int32 as G x 2 int64) | abc (G x 3) | sf (G x 2)]."""
+    key = (device.index,) + tuple(
+        (a.data_ptr(), b.data_ptr(), c.data_ptr(), sa.data_ptr(), sb.data_ptr()) + tuple(sz)
+        for (a, b, c), (sa, sb), sz in zip(abc, sfp, sizes))
+    t = _TABLE_CACHE.get(key)
+    if t is not None:
+        _TABLE_CACHE.move_to_end(key)
+        return t
+    G = len(sizes)
+    host = torch.empty(7 * G, dtype=torch.int64, pin_memory=True)
+    sz32 = host[: 2 * G].view(torch.int32)
+    sz32.copy_(torch.tensor([list(s) for s in sizes], dtype=torch.int32).reshape(-1))
+    host[2 * G: 5 * G] = torch.tensor([[a.data_ptr(), b.data_ptr(), c.data_ptr()] for a, b, c in abc],
+                                      dtype=torch.int64).reshape(-1)
+    host[5 * G: 7 * G] = torch.tensor([[sa.data_ptr(), sb.data_ptr()] for sa, sb in sfp],
+                                      dtype=torch.int64).reshape(-1)
+    t = host.to(device, non_blocking=True)
+    _TABLE_CACHE[key] = t
+    if len(_TABLE_CACHE) > _TABLE_CACHE_MAX:
+        _TABLE_CACHE.popitem(last=False)
+    return t
+
+
+def _workspace(G: int, device, stream) -> torch.Tensor:
+    key = (device.index, stream, G)
+    ws = _WORKSPACES.get(key)
+    if ws is None:
+        nbytes = _native.load().nvfp4_grouped_gemm_workspace_size(G)
+        ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def launch_tables(table: torch.Tensor, G: int, stream=None, opt=None) -> None:
+    """Launch on a prebuilt device table (see ``_table``)."""
+    lib = _native.load()
+    s = torch.cuda.current_stream().cuda_stream if stream is None else stream
+    ws = _workspace(G, table.device, s)
+    base = ws.data_ptr()
+    aligned = (base + 255) // 256 * 256
+    nbytes = ws.numel() - (aligned - base)
+    p = table.data_ptr()
+    args = (p, p + 16 * G, p + 40 * G, G, aligned, nbytes, s)
+    if opt is None:
+        rc = lib.nvfp4_grouped_gemm(*args)
+    else:
+        rc = lib.nvfp4_grouped_gemm_ex(*args, ctypes.byref(opt))
+    _native.check(rc, "nvfp4_grouped_gemm")
+
+
+def custom_kernel(data: group_input_t, opt=None) -> group_output_t:
+    abc, _, sfp, sizes = data
+    if len(abc) == 0:
+        return []
+    device = abc[0][0].device
+    for (a, b, c), (sa, sb), (m, n, k, l) in zip(abc, sfp, sizes):
+        if l != 1:
+            raise ValueError("grouped GEMM groups must have l == 1")
+        if tuple(a.shape) != (m, k // 2, 1) or tuple(b.shape) != (n, k // 2, 1):
+            raise ValueError(f"group operand shapes {tuple(a.shape)}, {tuple(b.shape)} do not match {(m, n, k)}")
+        if a.stride()[:2] != (k // 2, 1) and m > 1 or b.stride()[:2] != (k // 2, 1) and n > 1:
+            raise ValueError("group operands must be K-major")
+        if c.dtype != torch.float16 or tuple(c.shape) != (m, n, 1) or (m > 1 and c.stride()[0] != n):
+            raise ValueError("group outputs must be row-major float16 (m, n, 1)")
+        sf_k = ceil_div(k, SF_VEC)
+        if not is_permuted_layout(sa, m, sf_k, 1) or not is_permuted_layout(sb, n, sf_k, 1):
+            raise ValueError("scale tensors must use the permuted layout")
+    table = _table(abc, sfp, sizes, device)
+    launch_tables(table, len(sizes), opt=opt)
+    return [c for _, _, c in abc]

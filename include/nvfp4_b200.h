@@ -51,10 +51,13 @@ extern "C" {
 typedef struct nvfp4_options {
   int operand_order;              /* 0 = auto; 1 = A feeds the 128-row MMA side;
                                      2 = B feeds it ("swap", for skinny M) */
-  int tile_n;                     /* 0 = auto; else 32, 64, 128, 192 or 256 */
+  int tile_n;                     /* 0 = auto; else 64, 128 or 256 */
   int max_ctas;                   /* 0 = one CTA per SM */
   unsigned long long timeout_ns;  /* 0 = library default (2 s per pipeline wait) */
-  int debug_skip_producer;        /* test hook: issue no loads so every wait runs out */
+  int debug;                      /* test/probe bits, 0 in normal use: 1 = issue no loads so every
+                                     pipeline wait runs out (status test); 2/4/8/16 = skip data
+                                     movement / MMAs / scale stores / output stores (timing probes) */
+  void* trace;                    /* NULL, or device buffer of 6 x 256 uint64 timestamps (CTA 0) */
 } nvfp4_options;
 
 /* Human-readable message for the last error returned on this thread. */

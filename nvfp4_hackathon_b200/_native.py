@@ -52,7 +52,8 @@ class Nvfp4Options(ctypes.Structure):
         ("tile_n", ctypes.c_int),
         ("max_ctas", ctypes.c_int),
         ("timeout_ns", ctypes.c_ulonglong),
-        ("debug_skip_producer", ctypes.c_int),
+        ("debug", ctypes.c_int),
+        ("trace", ctypes.c_void_p),
     ]
 
 
@@ -126,5 +127,5 @@ def raise_on_device_error() -> None:
         raise Nvfp4Error(f"device-side error: {STATUS.get(s, s)}")
 
 
-def options(operand_order=0, tile_n=0, max_ctas=0, timeout_ns=0, debug_skip_producer=0):
-    return Nvfp4Options(operand_order, tile_n, max_ctas, timeout_ns, debug_skip_producer)
+def options(operand_order=0, tile_n=0, max_ctas=0, timeout_ns=0, debug=0, trace=None):
+    return Nvfp4Options(operand_order, tile_n, max_ctas, timeout_ns, debug, trace)

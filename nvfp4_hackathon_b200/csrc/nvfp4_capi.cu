@@ -185,7 +185,8 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   prm.q_fastest = 0;
   prm.status = st->status;
   prm.timeout_ns = (opt && opt->timeout_ns) ? opt->timeout_ns : g_timeout_ns;
-  prm.debug_skip_producer = opt ? opt->debug_skip_producer : 0;
+  prm.debug = opt ? opt->debug : 0;
+  prm.trace = opt ? reinterpret_cast<unsigned long long*>(opt->trace) : nullptr;
   int grid = st->num_sms;
   if (opt && opt->max_ctas > 0 && opt->max_ctas < grid) grid = opt->max_ctas;
   if (grid > prm.total_tiles) grid = prm.total_tiles;
@@ -320,7 +321,8 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   prm.tile_prefix = prefix;
   prm.status = st->status;
   prm.timeout_ns = (opt && opt->timeout_ns) ? opt->timeout_ns : g_timeout_ns;
-  prm.debug_skip_producer = opt ? opt->debug_skip_producer : 0;
+  prm.debug = opt ? opt->debug : 0;
+  prm.trace = opt ? reinterpret_cast<unsigned long long*>(opt->trace) : nullptr;
   int grid = st->num_sms;
   if (opt && opt->max_ctas > 0 && opt->max_ctas < grid) grid = opt->max_ctas;
   return launch<true, true, BN>(tp, tq, prm, grid, stream);
@@ -386,7 +388,6 @@ int nvfp4_gemm_ex(const void* a, const void* b, const void* sfa_perm, const void
   NVFP4_DENSE_CASE(true, 256)
   NVFP4_DENSE_CASE(false, 64)
   NVFP4_DENSE_CASE(false, 128)
-  NVFP4_DENSE_CASE(false, 192)
   NVFP4_DENSE_CASE(false, 256)
 #undef NVFP4_DENSE_CASE
   return fail(NVFP4_ERR_UNSUPPORTED, "no kernel for swap=%d tile_n=%d", (int)ch.swap, ch.bn);

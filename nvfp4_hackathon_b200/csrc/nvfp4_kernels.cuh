@@ -6,26 +6,35 @@
 //
 //     D[p, q] = sum_k  e2m1(P[p, k]) * sfP[p, k/16]  *  e2m1(Q[q, k]) * sfQ[q, k/16]
 //
-// in fp32 in tensor memory and stores fp16.  P is the operand that feeds the
-// 128-row MMA M side, Q the operand that feeds the MMA N side (BN rows).  For
-// the ordinary layout P = A (M rows) and Q = B (N rows) and C[m, n] = D[m, n];
-// for "swap" P = B and Q = A and C[m, n] = D[n, m], which lets a skinny M
-// (decode-like shapes, small MoE groups) sit on the flexible N side of the MMA.
+// with fp32 accumulation in tensor memory and stores fp16.  P is the operand
+// on the 128-row MMA M side, Q the operand on the MMA N side (BN rows).  For
+// the ordinary order P = A (M rows), Q = B (N rows) and C[m, n] = D[m, n]; for
+// "swap" P = B, Q = A and C[m, n] = D[n, m], which puts a skinny M (decode-like
+// shapes, small MoE groups) on the flexible N side of the MMA.
 //
-// Roles (192 threads):
-//   warps 0-3  epilogue: TMEM -> registers -> fp16 -> global (warp w owns TMEM lanes 32w..32w+31)
-//   warp 4     producer: TMA tiles of P and Q (128-byte swizzle) + bulk copies of the
-//              scale-factor atoms into an mbarrier ring of STAGES stages
-//   warp 5     TMEM owner and MMA issuer: tcgen05.cp scale atoms into TMEM, then
-//              tcgen05.mma kind::mxf4nvf4 (K = 64 per instruction, 4 per stage)
+// Roles (18 warps):
+//   warps 0-7   epilogue: warp w drains TMEM lanes 32*(w%4).. and column half w/4 of the
+//               accumulator into registers as fp16, releases the accumulator, then stores
+//               to global while the next tile's MMAs already run
+//   warp 8      producer: TMA loads of the P and Q tiles (128-byte swizzle) and plain bulk
+//               copies of the scale atoms into a ring of kStages shared-memory stages
+//   warp 9      TMEM owner and MMA issuer: tcgen05.mma kind::mxf4nvf4 (K = 64 per
+//               instruction), one tcgen05.commit per stage to release it.
+//   warps 10-17 scale warps, two groups of four (group g serves stages with s % 2 == g):
+//               each warp moves the stage's scale atoms from shared memory into its own 32
+//               TMEM lanes with ld.shared + tcgen05.st.  (tcgen05.cp costs ~115 cycles per
+//               512-byte atom on the copy engine; register stores run alongside the MMAs.)
+//               Scale buffer s belongs to stage s, so "stage s refilled" already implies
+//               that the MMAs that read the buffer's previous contents have finished.
 //
 // Scale factors arrive in the reference's pre-permuted layout
 // (kernels/gemm/reference.py:113-150): per 128-row block and per 64-wide K block
 // one 512-byte atom whose byte (r % 32) * 16 + (r / 32) * 4 + j holds row r,
-// K-vector j.  The four atoms of one 256-wide K stage are contiguous (2 KiB),
-// so they are fetched with one plain bulk copy, and tcgen05.cp 32x128b.warpx4
-// puts an atom into four TMEM columns in exactly the order the MMA reads it
-// (column c, lane l <-> row 32c + l).
+// K-vector j.  The four atoms of one 256-wide K stage are contiguous (2 KiB) and
+// arrive with one bulk copy.  The MMA reads the scales of row r from TMEM column
+// (r / 32), lane (r % 32) of every lane quarter, so every scale warp stores atom
+// row `lane` (16 bytes = 4 columns) into its own quarter: the same bytes land in
+// all four quarters.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -37,38 +46,43 @@ namespace nvfp4 {
 constexpr int kBM = 128;            // MMA M (rows of P per tile)
 constexpr int kBKBytes = 128;       // bytes of K per stage (256 fp4 values)
 constexpr int kBK = 256;            // K elements per stage
-constexpr int kMmaK = 64;           // K per tcgen05.mma
 constexpr int kAtomBytes = 512;     // one scale-factor atom: 128 rows x 4 K-vectors
-constexpr int kNumThreads = 192;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
+constexpr int kEpiWarps = 8;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kFirstSfWarp = 10;
+constexpr int kSfGroups = 2;        // groups of 4 scale warps; group g serves stages s % 2 == g
+constexpr int kNumThreads = 32 * (kFirstSfWarp + 4 * kSfGroups);
 constexpr int kSmemBudget = 232448 - 2048;  // dynamic smem per CTA minus alignment/barriers
 
 template <int BN>
 struct Cfg {
-  static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 192 || BN == 256,
-                "BN must be 32, 64, 128, 192 or 256 (tiles start on 32-row boundaries of a scale block)");
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
   static constexpr int kPBytes = kBM * kBKBytes;
   static constexpr int kQBytes = BN * kBKBytes;
-  // 128-row scale blocks a Q tile can touch (a tile may start at row 64 of a block).
-  static constexpr int kSfqAtoms = (BN <= 128) ? 1 : 2;
+  static constexpr int kSfqAtoms = (BN <= 128) ? 1 : 2;  // 128-row scale blocks per Q tile
   static constexpr int kSfpBytes = 4 * kAtomBytes;
   static constexpr int kSfqBytes = kSfqAtoms * 4 * kAtomBytes;
   static constexpr int kStageBytes = kPBytes + kQBytes + kSfpBytes + kSfqBytes;
-  static constexpr int kStagesRaw = kSmemBudget / kStageBytes;
-  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr int kSfqColsPerKb = 4 * kSfqAtoms;
-  static constexpr int kSfCols = 4 * 4 + 4 * kSfqColsPerKb;
-  static constexpr int kAccStages = (2 * BN + kSfCols <= 512) ? 2 : 1;
-  static constexpr int kColsNeeded = kAccStages * BN + kSfCols;
+  // TMEM columns of one scale buffer: [SFP kb0..kb3 (16 columns)][SFQ kb0..kb3]
+  static constexpr int kSfCols = 16 + 4 * kSfqColsPerKb;
+  static constexpr int kAccStages = (BN <= 128) ? 2 : 1;
+  // one scale buffer per stage; stages come in pairs released by one commit
+  static constexpr int kStagesSmem = kSmemBudget / kStageBytes;
+  static constexpr int kStagesTmem = (512 - kAccStages * BN) / kSfCols;
+  static constexpr int kStagesRaw = kStagesSmem < kStagesTmem ? kStagesSmem : kStagesTmem;
+  static constexpr int kStagesCap = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static constexpr int kStages = kStagesCap & ~1;  // even: the two scale-warp groups alternate
+  static constexpr int kColsNeeded = kAccStages * BN + kStages * kSfCols;
   static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64
                                  : kColsNeeded <= 128 ? 128 : kColsNeeded <= 256 ? 256 : 512;
-  static constexpr int kSfpCol = kAccStages * BN;
-  static constexpr int kSfqCol = kSfpCol + 16;
-  // barriers: full[S], empty[S], acc_full[A], acc_empty[A], drain; then tmem ptr + abort flag
-  static constexpr int kBarrierBytes = 8 * (2 * kStages + 2 * kAccStages + 1) + 16;
+  static constexpr int kSfCol0 = kAccStages * BN;
+  // barriers: full[S], sf_full[S/2], empty[S], acc_full[A], acc_empty[A], drain
+  static constexpr int kNumBars = 2 * kStages + kStages / 2 + 2 * kAccStages + 1;
+  static constexpr int kBarrierBytes = 8 * kNumBars + 16;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
-  static_assert(kStages >= 2, "not enough shared memory for two stages");
+  static_assert(kStages >= 2 && kStages % 2 == 0, "need an even number of stages");
   static_assert(kColsNeeded <= 512, "TMEM budget exceeded");
 };
 
@@ -96,8 +110,25 @@ struct GemmParams {
   // control
   int* status;
   unsigned long long timeout_ns;
-  int debug_skip_producer;      // test hook: producer issues nothing, waits must time out
+  // Probe bits (timing experiments and the timeout test; 0 in normal use):
+  //   1 producer issues nothing (every wait must time out)   2 no data movement
+  //   4 no MMAs   8 no scale stores   16 no epilogue stores
+  int debug;
+  // When non-null, CTA 0 records %globaltimer stamps of its pipeline events here
+  // (slot layout in trace_slot()); used to measure hand-off latencies.
+  unsigned long long* trace;
 };
+
+// trace slots: role r (0 producer, 1 mma-wait-done, 2 mma-issued, 3 sf-group0 done,
+// 4 sf-group1 done, 5 epilogue tile done) x step (< kTraceSteps)
+// (slots 6 x 256 hold the matching clock64 values)
+constexpr int kTraceSteps = 256;
+__device__ __forceinline__ void trace_event(const GemmParams& prm, int role, uint32_t step) {
+  if (prm.trace && blockIdx.x == 0 && step < (uint32_t)kTraceSteps) {
+    prm.trace[role * kTraceSteps + step] = global_timer_ns();
+    prm.trace[(6 + role) * kTraceSteps + step] = clock64();
+  }
+}
 
 // Per-tile view shared by all roles.
 struct TileInfo {
@@ -185,22 +216,21 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_addr);
 
-  // stage s: [P | Q | SFP | SFQ]
-  auto stage_p = [&](int s) { return base + s * C_::kStageBytes; };
-  auto stage_q = [&](int s) { return base + s * C_::kStageBytes + C_::kPBytes; };
-  auto stage_sfp = [&](int s) { return base + s * C_::kStageBytes + C_::kPBytes + C_::kQBytes; };
-  auto stage_sfq = [&](int s) {
-    return base + s * C_::kStageBytes + C_::kPBytes + C_::kQBytes + C_::kSfpBytes;
-  };
+  // stage s: [P | Q | SFP atoms | SFQ atoms]
+  auto stage_off = [&](int s) { return (uint32_t)(s * C_::kStageBytes); };
+  constexpr uint32_t kOffQ = C_::kPBytes;
+  constexpr uint32_t kOffSfp = C_::kPBytes + C_::kQBytes;
+  constexpr uint32_t kOffSfq = kOffSfp + C_::kSfpBytes;
   const uint32_t bar_base = base + S * C_::kStageBytes;
   auto full_bar = [&](int s) { return bar_base + 8 * s; };
-  auto empty_bar = [&](int s) { return bar_base + 8 * (S + s); };
-  auto accf_bar = [&](int a) { return bar_base + 8 * (2 * S + a); };
-  auto acce_bar = [&](int a) { return bar_base + 8 * (2 * S + A + a); };
-  const uint32_t drain_bar = bar_base + 8 * (2 * S + 2 * A);
+  auto sff_bar = [&](int s) { return bar_base + 8 * (S + (s >> 1)); };  // one per stage pair
+  auto empty_bar = [&](int s) { return bar_base + 8 * (S + S / 2 + s); };
+  auto accf_bar = [&](int a) { return bar_base + 8 * (2 * S + S / 2 + a); };
+  auto acce_bar = [&](int a) { return bar_base + 8 * (2 * S + S / 2 + A + a); };
+  const uint32_t drain_bar = bar_base + 8 * (2 * S + S / 2 + 2 * A);
   uint8_t* bar_ptr = smem + S * C_::kStageBytes;
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bar_ptr + 8 * (2 * S + 2 * A + 1));
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + 8 * (2 * S + 2 * A + 1) + 4);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bar_ptr + 8 * C_::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + 8 * C_::kNumBars + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -210,9 +240,10 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
+    for (int s = 0; s < S; s += 2) mbar_init(sff_bar(s), 4);  // one arrive per scale warp
     for (int a = 0; a < A; ++a) {
       mbar_init(accf_bar(a), 1);
-      mbar_init(acce_bar(a), 128);
+      mbar_init(acce_bar(a), 32 * kEpiWarps);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -234,17 +265,29 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
 
   const int total = GROUPED ? __ldg(prm.tile_prefix + prm.G) : prm.total_tiles;
   const uint64_t tmo = prm.timeout_ns;
+  // scale atoms a Q tile needs (it may start at row 32, 64 or 96 of a 128-row block)
+  auto q_atoms = [&](const TileInfo& ti) {
+    const int rq = (ti.q_rows + 127) >> 7;
+    int nq = ((ti.q0 & 127) + BN + 127) >> 7;
+    if (nq > C_::kSfqAtoms) nq = C_::kSfqAtoms;
+    if ((ti.q0 >> 7) + nq > rq) nq = rq - (ti.q0 >> 7);
+    return nq;
+  };
+  auto k_blocks = [&](const TileInfo& ti, int kt) {
+    const int kbv = ti.rk - kt * 4;
+    return kbv > 4 ? 4 : kbv;
+  };
 
   if (warp == kProducerWarp) {
-    if (lane == 0 && !prm.debug_skip_producer) {
+    if (lane == 0 && !(prm.debug & 1)) {
       // ------------------------------------------------------------ producer
-      const uint64_t pol_stream = policy_evict_first();
       const uint64_t pol_keep = policy_evict_last();
       int s = 0;
       uint32_t ph = 0;
       const void* last_map = nullptr;
       bool ok = true;
       uint32_t issued_mask = 0, issued_par = 0;
+      uint32_t pstep = 0;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         TileInfo ti;
         decode_tile<GROUPED, SWAP, BN>(prm, &tm_p, &tm_q, t, ti);
@@ -255,30 +298,28 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         }
         const int pblk = ti.p0 >> 7;
         const int qblk = ti.q0 >> 7;
-        const int rq = (ti.q_rows + 127) >> 7;
-        int nq_atoms = ((ti.q0 & 127) + BN + 127) >> 7;
-        if (nq_atoms > C_::kSfqAtoms) nq_atoms = C_::kSfqAtoms;
-        if (qblk + nq_atoms > rq) nq_atoms = rq - qblk;
-        // P (the operand re-read by several tiles in flight) stays in L2 longer
-        const uint64_t pol_p = pol_keep;
-        const uint64_t pol_q = pol_stream;
-        (void)pol_q;
+        const int nq_atoms = q_atoms(ti);
         for (int kt = 0; kt < ti.num_kt; ++kt) {
           if (!mbar_wait_bounded(empty_bar(s), ph ^ 1, abort_flag, prm.status,
                                  kStatusTimeoutProducer, tmo)) { ok = false; break; }
-          int kbv = ti.rk - kt * 4;
-          if (kbv > 4) kbv = 4;
-          const uint32_t sf_bytes = kbv * kAtomBytes;
+          if (prm.debug & 2) {  // timing probe: no data movement
+            mbar_arrive(full_bar(s));
+            if (++s == S) { s = 0; ph ^= 1; }
+            continue;
+          }
+          const uint32_t sf_bytes = k_blocks(ti, kt) * kAtomBytes;
           const uint32_t bytes = C_::kPBytes + C_::kQBytes + sf_bytes * (1 + nq_atoms);
+          const uint32_t st = base + stage_off(s);
           mbar_arrive_expect_tx(full_bar(s), bytes);
-          tma_load_3d(stage_p(s), ti.map_p, full_bar(s), kt * kBKBytes, ti.p0, ti.l, pol_p);
-          tma_load_3d(stage_q(s), ti.map_q, full_bar(s), kt * kBKBytes, ti.q0, ti.l, pol_keep);
-          bulk_load(stage_sfp(s), ti.sf_p + ((long long)pblk * ti.rk + kt * 4) * kAtomBytes,
+          tma_load_3d(st, ti.map_p, full_bar(s), kt * kBKBytes, ti.p0, ti.l, pol_keep);
+          tma_load_3d(st + kOffQ, ti.map_q, full_bar(s), kt * kBKBytes, ti.q0, ti.l, pol_keep);
+          bulk_load(st + kOffSfp, ti.sf_p + ((long long)pblk * ti.rk + kt * 4) * kAtomBytes,
                     sf_bytes, full_bar(s), pol_keep);
           for (int a = 0; a < nq_atoms; ++a)
-            bulk_load(stage_sfq(s) + a * 4 * kAtomBytes,
+            bulk_load(st + kOffSfq + a * 4 * kAtomBytes,
                       ti.sf_q + ((long long)(qblk + a) * ti.rk + kt * 4) * kAtomBytes, sf_bytes,
                       full_bar(s), pol_keep);
+          trace_event(prm, 0, pstep++);
           issued_mask |= 1u << s;
           issued_par = (issued_par & ~(1u << s)) | (ph << s);
           if (++s == S) { s = 0; ph ^= 1; }
@@ -294,11 +335,12 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       // ------------------------------------------------------------ MMA issuer
-      int s = 0;
-      uint32_t ph = 0;
+      bool ok = true;
       int acc = 0;
       uint32_t aph = 0;
-      bool ok = true;
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t step = 0;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         TileInfo ti;
         decode_tile<GROUPED, SWAP, BN>(prm, &tm_p, &tm_q, t, ti);
@@ -308,39 +350,42 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         const uint32_t idesc = make_idesc_mxf4nvf4(kBM, n_mma);
         const uint32_t d_tmem = tmem_base + acc * BN;
         const uint32_t sfq_shift = (ti.q0 & 127) >> 5;
-        const int rq = (ti.q_rows + 127) >> 7;
-        int nq_atoms = ((ti.q0 & 127) + BN + 127) >> 7;
-        if (nq_atoms > C_::kSfqAtoms) nq_atoms = C_::kSfqAtoms;
-        if ((ti.q0 >> 7) + nq_atoms > rq) nq_atoms = rq - (ti.q0 >> 7);
-        if (!mbar_wait_bounded(acce_bar(acc), aph ^ 1, abort_flag, prm.status, kStatusTimeoutMma,
+        if (!(prm.debug & 8192) &&
+            !mbar_wait_bounded(acce_bar(acc), aph ^ 1, abort_flag, prm.status, kStatusTimeoutMma,
                                tmo)) { ok = false; break; }
         tc_fence_after();
-        for (int kt = 0; kt < ti.num_kt; ++kt) {
-          if (!mbar_wait_bounded(full_bar(s), ph, abort_flag, prm.status, kStatusTimeoutMma, tmo)) {
-            ok = false;
-            break;
+        for (int kt = 0; kt < ti.num_kt; ++kt, ++step) {
+          // One wait per stage pair: the scale warps arrive on sf_full only after both
+          // stages' data landed and both scale buffers are written.  (Any mbarrier wait
+          // in this thread costs ~130 cycles after a tcgen05.commit, so halve them.)
+          if (!(s & 1)) {
+            if (!mbar_wait_bounded(sff_bar(s), ph, abort_flag, prm.status, kStatusTimeoutMma, tmo)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
           }
-          tc_fence_after();
-          int kbv = ti.rk - kt * 4;
-          if (kbv > 4) kbv = 4;
-          for (int kb = 0; kb < kbv; ++kb) {
-            tc_cp_32x128b_warpx4(tmem_base + C_::kSfpCol + kb * 4,
-                                 make_smem_desc(stage_sfp(s) + kb * kAtomBytes, 0, 128, 0));
-            for (int a = 0; a < nq_atoms; ++a)
-              tc_cp_32x128b_warpx4(
-                  tmem_base + C_::kSfqCol + kb * C_::kSfqColsPerKb + a * 4,
-                  make_smem_desc(stage_sfq(s) + a * 4 * kAtomBytes + kb * kAtomBytes, 0, 128, 0));
+          trace_event(prm, 1, step);
+          const uint32_t sfp_col = tmem_base + C_::kSfCol0 + s * C_::kSfCols;
+          const uint32_t sfq_col = sfp_col + 16 + sfq_shift;
+          const uint64_t pdesc = make_smem_desc(base + stage_off(s), 0, 1024, 2);
+          const uint64_t qdesc = make_smem_desc(base + stage_off(s) + kOffQ, 0, 1024, 2);
+          const uint32_t acc0 = kt > 0 ? 1u : 0u;
+          if (prm.debug & 4) {
+          } else if (k_blocks(ti, kt) == 4) {
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb)
+              tc_mma_mxf4nvf4(d_tmem, pdesc + 2 * kb, qdesc + 2 * kb, idesc, sfp_col + kb * 4,
+                              sfq_col + kb * C_::kSfqColsPerKb, kb > 0 ? 1u : acc0);
+          } else {
+            const int kbv = k_blocks(ti, kt);
+            for (int kb = 0; kb < kbv; ++kb)
+              tc_mma_mxf4nvf4(d_tmem, pdesc + 2 * kb, qdesc + 2 * kb, idesc, sfp_col + kb * 4,
+                              sfq_col + kb * C_::kSfqColsPerKb, kb > 0 ? 1u : acc0);
           }
-          const uint64_t pdesc = make_smem_desc(stage_p(s), 0, 1024, 2);
-          const uint64_t qdesc = make_smem_desc(stage_q(s), 0, 1024, 2);
-          for (int kb = 0; kb < kbv; ++kb) {
-            // advance 32 bytes (64 fp4) along K inside the 128-byte swizzled row
-            tc_mma_mxf4nvf4(d_tmem, pdesc + 2 * kb, qdesc + 2 * kb, idesc,
-                            tmem_base + C_::kSfpCol + kb * 4,
-                            tmem_base + C_::kSfqCol + kb * C_::kSfqColsPerKb + sfq_shift,
-                            (kt > 0 || kb > 0) ? 1u : 0u);
-          }
+          // release the stage (and its scale buffer) once these MMAs have read it
           tc_commit(empty_bar(s));
+          trace_event(prm, 2, step);
           if (++s == S) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
@@ -351,63 +396,173 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       tc_commit(drain_bar);
       mbar_wait_bounded(drain_bar, 0, abort_flag, prm.status, kStatusTimeoutDrain, tmo);
     }
+  } else if (warp >= kFirstSfWarp) {
+    if (!(prm.debug & 4096)) {  // (probe bit 4096: scale warps idle)
+    // -------------------------------------------------------------- scale warps
+    // Group g serves stage pair g (stages 2g, 2g+1), group 1-g the next pair, and
+    // so on around the ring.  A warp waits for the pair's data, writes both scale
+    // buffers into its TMEM quarter, then arrives once on the pair's sf_full.
+    const int grp = (warp - kFirstSfWarp) >> 2;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM quarter
+    uint32_t tstep = 0;
+    int s = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    auto write_stage = [&](const TileInfo& ti, int kt, int cs, int nq_atoms) {
+      const int kbv = k_blocks(ti, kt);
+      const uint32_t col = tmem_base + lane_base + C_::kSfCol0 + cs * C_::kSfCols;
+      const uint8_t* sp = smem + stage_off(cs) + kOffSfp + lane * 16;
+      uint32_t r[16];
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (kb < kbv) v = *reinterpret_cast<const uint4*>(sp + kb * kAtomBytes);
+        r[4 * kb + 0] = v.x; r[4 * kb + 1] = v.y; r[4 * kb + 2] = v.z; r[4 * kb + 3] = v.w;
+      }
+      tmem_st_32x32b_x16(col, r);
+      const uint8_t* sq = smem + stage_off(cs) + kOffSfq + lane * 16;
+      if constexpr (C_::kSfqAtoms == 1) {
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb) {
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (kb < kbv) v = *reinterpret_cast<const uint4*>(sq + kb * kAtomBytes);
+          r[4 * kb + 0] = v.x; r[4 * kb + 1] = v.y; r[4 * kb + 2] = v.z; r[4 * kb + 3] = v.w;
+        }
+        tmem_st_32x32b_x16(col + 16, r);
+      } else {
+        uint32_t q[32];
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb)
+#pragma unroll
+          for (int a = 0; a < 2; ++a) {
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (kb < kbv && a < nq_atoms)
+              v = *reinterpret_cast<const uint4*>(sq + a * 4 * kAtomBytes + kb * kAtomBytes);
+            const int o = kb * 8 + a * 4;
+            q[o + 0] = v.x; q[o + 1] = v.y; q[o + 2] = v.z; q[o + 3] = v.w;
+          }
+        tmem_st_32x32b_x32(col + 16, q);
+      }
+    };
+    // The pair a k-stage belongs to is tracked across tiles: a pair can straddle
+    // two tiles when a tile has an odd number of k-stages.
+    TileInfo pend_ti;
+    int pend_kt = -1, pend_nq = 0;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      TileInfo ti;
+      decode_tile<GROUPED, SWAP, BN>(prm, &tm_p, &tm_q, t, ti);
+      const int nq_atoms = q_atoms(ti);
+      for (int kt = 0; kt < ti.num_kt && ok; ++kt, ++tstep) {
+        const int cs = s;
+        const uint32_t cph = ph;
+        if (++s == S) { s = 0; ph ^= 1; }
+        if (((cs >> 1) & 1) != grp) continue;
+        const bool last = (kt == ti.num_kt - 1) && (t + (int)gridDim.x >= total);
+        if (!(cs & 1) && !last) {  // first stage of the pair: remember it, handle with the second
+          pend_ti = ti;
+          pend_kt = kt;
+          pend_nq = nq_atoms;
+          continue;
+        }
+        int w_ok = 1;
+        if (lane == 0) {
+          if (cs & 1)
+            w_ok = mbar_wait_bounded(full_bar(cs - 1), cph, abort_flag, prm.status, kStatusTimeoutMma, tmo);
+          w_ok = w_ok && mbar_wait_bounded(full_bar(cs), cph, abort_flag, prm.status, kStatusTimeoutMma, tmo);
+        }
+        w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+        if (!w_ok) { ok = false; break; }
+        tc_fence_after();
+        if (!(prm.debug & 8)) {
+          if (cs & 1) write_stage(pend_ti, pend_kt, cs - 1, pend_nq);
+          write_stage(ti, kt, cs, nq_atoms);
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(sff_bar(cs));
+          if ((warp & 3) == 0) trace_event(prm, 3 + grp, tstep);
+        }
+      }
+    }
+    }
   } else {
+    if (!(prm.debug & 8192)) {  // (probe bit 8192: epilogue idle)
     // -------------------------------------------------------------- epilogue
+    // Warp w owns accumulator rows 32*(w%4).. and columns [h*BN/2, (h+1)*BN/2), h = w/4.
+    // It pulls its whole slice out of TMEM as packed fp16 first, releases the
+    // accumulator, and only then writes global memory.
+    constexpr int kHalf = BN / 2;
+    constexpr int kChunks = kHalf / 32;
     int acc = 0;
     uint32_t aph = 0;
-    const int row = warp * 32 + lane;  // TMEM lane == accumulator row
+    uint32_t etile = 0;
+    const int quad = warp & 3;
+    const int half = warp >> 2;
+    const int row = quad * 32 + lane;  // TMEM lane == accumulator row
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       TileInfo ti;
       decode_tile<GROUPED, SWAP, BN>(prm, &tm_p, &tm_q, t, ti);
       if (!mbar_wait_bounded(accf_bar(acc), aph, abort_flag, prm.status, kStatusTimeoutEpilogue,
                              tmo)) break;
       tc_fence_after();
-      const int p = ti.p0 + row;
-      const bool p_ok = p < ti.p_rows;
-      const uint32_t t_row = tmem_base + ((uint32_t)(warp * 32) << 16) + acc * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int qc = ti.q0 + c * 32;
-        if (qc >= ti.q_rows) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        tmem_ld_wait();
-        if (!p_ok) continue;
-        if constexpr (!SWAP) {
-          __half* dst = ti.C + (long long)p * ti.ldc + qc;
-          const bool full = (qc + 32 <= ti.q_rows) &&
-                            ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
-          if (full) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst);
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + half * kHalf;
+      const int q_lo = ti.q0 + half * kHalf;
+      uint32_t pk[kChunks][16];
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              __half2 h0 = __floats2half2_rn(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
-              __half2 h1 = __floats2half2_rn(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
-              __half2 h2 = __floats2half2_rn(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
-              __half2 h3 = __floats2half2_rn(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
-              w.x = *reinterpret_cast<uint32_t*>(&h0);
-              w.y = *reinterpret_cast<uint32_t*>(&h1);
-              w.z = *reinterpret_cast<uint32_t*>(&h2);
-              w.w = *reinterpret_cast<uint32_t*>(&h3);
-              d4[v] = w;
+      for (int c = 0; c < kChunks; ++c) {
+        if (q_lo + c * 32 < ti.q_rows && !(prm.debug & 64)) {  // warp-uniform
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(t_row + c * 32 + hh * 16, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              __half2 h = __floats2half2_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+              pk[c][hh * 8 + j] = *reinterpret_cast<uint32_t*>(&h);
             }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (qc + j < ti.q_rows) dst[j] = __float2half_rn(__uint_as_float(r[j]));
           }
-        } else {
-          // D[p=n, q=m] -> C[m, n]; lanes hold consecutive n, so each store is warp-coalesced
-          __half* dst = ti.C + (long long)qc * ti.ldc + p;
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (qc + j < ti.q_rows) dst[(long long)j * ti.ldc] = __float2half_rn(__uint_as_float(r[j]));
         }
       }
       tc_fence_before();
       mbar_arrive(acce_bar(acc));
+      if (threadIdx.x == 0) trace_event(prm, 5, etile++);
       if (++acc == A) { acc = 0; aph ^= 1; }
+      const int p = ti.p0 + row;
+      if (p < ti.p_rows && !(prm.debug & 16)) {
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+          const int qc = q_lo + c * 32;
+          if (qc >= ti.q_rows) break;
+          if constexpr (!SWAP) {
+            __half* dst = ti.C + (long long)p * ti.ldc + qc;
+            if (qc + 32 <= ti.q_rows && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                d4[v] = make_uint4(pk[c][4 * v], pk[c][4 * v + 1], pk[c][4 * v + 2], pk[c][4 * v + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (qc + j < ti.q_rows)
+                  dst[j] = (j & 1) ? __high2half(*reinterpret_cast<__half2*>(&pk[c][j >> 1]))
+                                   : __low2half(*reinterpret_cast<__half2*>(&pk[c][j >> 1]));
+            }
+          } else {
+            // D[p=n, q=m] -> C[m, n]; lanes hold consecutive n, so each store is warp-coalesced
+            __half* dst = ti.C + (long long)qc * ti.ldc + p;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (qc + j < ti.q_rows)
+                dst[(long long)j * ti.ldc] =
+                    (j & 1) ? __high2half(*reinterpret_cast<__half2*>(&pk[c][j >> 1]))
+                            : __low2half(*reinterpret_cast<__half2*>(&pk[c][j >> 1]));
+          }
+        }
+      }
+    }
     }
   }
 

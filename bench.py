@@ -1,0 +1,498 @@
+#!/usr/bin/env python3
+"""Benchmark of the NVFP4 GEMM / grouped-GEMM hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1] [--impl ours|reference]
+
+One "step" is one call of the hot path over one batch of synthetic input.
+Default workload: configs[1] of BASELINE.json (M=64, N=14336, K=4096, L=1), one
+replica per GPU (the dense GEMM does not shard; scaling "weak").  Other
+workloads: c0, c2 (dense), c3 (grouped G=8), c4a (grouped G=64, experts sharded
+across ranks, strong scaling), c4b (dense 16384x28672x8192 sharded along N,
+strong scaling; ``--gather`` adds the NCCL all-gather of C).
+
+Prints one JSON line on rank 0.  ``value`` is the kernel throughput with inputs
+resident in HBM (L2 flushed by a 256 MiB write before every step; each call is
+timed with CUDA events on the launching stream, max over ranks); ``e2e`` is the
+same metric through ``custom_kernel`` with pinned host buffers and the
+host<->device copies inside the timed region.  ``--impl reference`` times the
+reference semantics on the host cores (the CPU restatement under ``oracle/``;
+the reference itself has no CPU implementation: its ``ref_kernel`` calls
+torch._scaled_mm on CUDA).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "nvfp4_gemm_tflops"
+UNIT = "TFLOP/s"
+FLUSH_BYTES = 256 * 1024 * 1024
+
+WORKLOADS = {
+    "c0": dict(kind="dense", m=128, n=256, k=512, desc="configs[0] M=128 N=256 K=512 L=1"),
+    "c1": dict(kind="dense", m=64, n=14336, k=4096, desc="configs[1] M=64 N=14336 K=4096 L=1"),
+    "c2": dict(kind="dense", m=8192, n=8192, k=8192, desc="configs[2] M=N=K=8192 L=1"),
+    "c3": dict(kind="grouped", g=8, n=4096, k=7168, desc="configs[3] G=8 N=4096 K=7168 M_g~U{64..1024}"),
+    "c4a": dict(kind="grouped_sharded", g=64, n=2048, k=7168, tokens=32768,
+                desc="configs[4a] G=64 N=2048 K=7168 sum(M)=32768 Zipf(1.1), experts sharded"),
+    "c4b": dict(kind="dense_sharded", m=16384, n=28672, k=8192,
+                desc="configs[4b] M=16384 N=28672 K=8192, N sharded"),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", default="c1", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--gather", action="store_true", help="c4b: all-gather C shards (NCCL)")
+    ap.add_argument("--e2e-steps", type=int, default=0, help="0 = min(steps, 50)")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline budget")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- helpers
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic(kernel_tag: str):
+    """DRAM bytes per launch recorded from an ncu capture (profiles/<tag>.txt,
+    line 'dram_bytes_per_launch: N'), or None."""
+    path = os.path.join(ROOT, "profiles", kernel_tag + ".txt")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+
+    def summary(self, t0: float, t1: float):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ts, line in self.lines:
+            if not (t0 - 0.15 <= ts <= t1 + 0.15):
+                continue
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workloads
+def dense_flops(m, n, k):
+    return 2.0 * m * n * k
+
+
+def dense_bytes(m, n, k):
+    """Algorithmic bytes: A + B codes, their e4m3 scales (unpadded), fp16 C."""
+    return m * k // 2 + n * k // 2 + m * (k // 16) + n * (k // 16) + 2 * m * n
+
+
+def grouped_flops(ms, n, k):
+    return sum(2.0 * m * n * k for m in ms)
+
+
+def grouped_bytes(ms, n, k):
+    live = [m for m in ms if m > 0]
+    return len(live) * (n * k // 2 + n * (k // 16)) + sum(m * (k // 2 + k // 16 + 2 * n) for m in live)
+
+
+class Workload:
+    """Device inputs for one rank plus the callable that runs one step."""
+
+    def __init__(self, name, rank, world, device, gather=False):
+        import torch
+        from nvfp4_hackathon_b200 import gemm, group_gemm, inputs, sharding
+        self.name = name
+        w = WORKLOADS[name]
+        self.desc = w["desc"]
+        self.kind = w["kind"]
+        seed = 1111
+        if self.kind == "dense":
+            m, n, k = w["m"], w["n"], w["k"]
+            self.data = inputs.generate_quantized_input(m, n, k, 1, seed=seed + rank, device=device)
+            self.flops = dense_flops(m, n, k)
+            self.bytes = dense_bytes(m, n, k)
+            self.run = lambda: gemm.custom_kernel(self.data)
+            self.scaling = "weak"
+            self.global_flops = self.flops * world
+            self.launches_per_step = 1
+        elif self.kind == "dense_sharded":
+            m, n, k = w["m"], w["n"], w["k"]
+            lo, hi = sharding.column_shard(n, world, rank)
+            self.data = inputs.generate_quantized_input(m, hi - lo, k, 1, seed=seed + rank, device=device)
+            self.flops = dense_flops(m, hi - lo, k)
+            self.bytes = dense_bytes(m, hi - lo, k)
+            self.global_flops = dense_flops(m, n, k)
+            self.scaling = "strong"
+            self.launches_per_step = 1
+            if gather and world > 1:
+                import torch.distributed as dist
+                lo0, hi0 = sharding.column_shard(n, world, 0)
+                gathered = torch.empty((world, m, hi0 - lo0), dtype=torch.float16, device=device)
+
+                def run():
+                    c = gemm.custom_kernel(self.data)
+                    sharding.gather_columns(c[:, :, 0], gathered, dist)
+                    return c
+                self.run = run
+            else:
+                self.run = lambda: gemm.custom_kernel(self.data)
+        else:
+            n, k = w["n"], w["k"]
+            if self.kind == "grouped":
+                ms = inputs.uniform_group_sizes(w["g"], seed=seed)
+                self.scaling = "weak"
+                self.global_flops = grouped_flops(ms, n, k) * world
+                local = ms
+            else:
+                ms = inputs.zipf_group_sizes(w["g"], w["tokens"])
+                plan = sharding.plan_expert_shards(ms, world, n=n, k=k)
+                local = [hi - lo for (_, lo, hi) in plan[rank]]
+                self.scaling = "strong"
+                self.global_flops = grouped_flops(ms, n, k)
+            self.ms = local
+            self.data = inputs.generate_quantized_group_input(local, n, k, seed=seed + rank, device=device)
+            self.flops = grouped_flops(local, n, k)
+            self.bytes = grouped_bytes(local, n, k)
+            self.run = lambda: group_gemm.custom_kernel(self.data)
+            self.launches_per_step = 2  # schedule/tensor-map prep + persistent GEMM
+        # FP4 peak ~4x the measured bf16 GEMM rate; HBM-bound if the intensity is below the ridge
+        hbm, bf16, _ = measured_peaks()
+        ridge = 4.0 * bf16 * 1e12 / (hbm * 1e9)
+        self.bound = "tensor" if self.flops / max(self.bytes, 1) > ridge else "hbm"
+
+
+def _storage_view(t):
+    """A flat uint8 view over the tensor's whole storage (the layouts here are dense)."""
+    import torch
+    n = t.untyped_storage().nbytes()
+    return torch.empty(0, dtype=torch.uint8, device=t.device).set_(t.untyped_storage(), 0, (n,), (1,))
+
+
+def _step_inputs(wl):
+    if wl.kind.startswith("dense"):
+        a, b, _, _, sfa, sfb, _ = wl.data
+        return [_storage_view(x) for x in (a, b, sfa, sfb)]
+    abc, _, sfp, _ = wl.data
+    out = []
+    for (a, b, _), (sa, sb) in zip(abc, sfp):
+        out += [_storage_view(x) for x in (a, b, sa, sb)]
+    return out
+
+
+def _step_outputs(wl):
+    if wl.kind.startswith("dense"):
+        return [_storage_view(wl.data[6])]
+    return [_storage_view(c) for _, _, c in wl.data[0]]
+
+
+# ----------------------------------------------------------------------------- our arm
+def bench_ours(args):
+    import torch
+    import torch.distributed as dist
+    from nvfp4_hackathon_b200 import _native
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    _native.load()
+    _native.status_reset()
+    wl = Workload(args.config, rank, world, device, gather=args.gather)
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=device)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
+        flush.fill_(1)
+        wl.run()
+    barrier()
+    _native.raise_on_device_error()
+
+    sampler = ClockSampler(local)
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)  # let the sampler start before the timed region
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier()
+    t_wall0 = time.time()
+    for s, e in ev:
+        flush.fill_(1)          # L2 flush before every step (outside the events)
+        s.record(stream)
+        wl.run()
+        e.record(stream)
+    barrier()
+    kernel_ms = [s.elapsed_time(e) for s, e in ev]
+    t = torch.tensor([sum(kernel_ms)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    _native.raise_on_device_error()
+
+    # ---------------------------------------------------------------- e2e (host buffers)
+    e2e_steps = args.e2e_steps or min(args.steps, 50)
+    dev_in = _step_inputs(wl)
+    host_in = []
+    for d in dev_in:
+        h = torch.empty(d.numel(), dtype=torch.uint8, pin_memory=True)
+        h.copy_(d.cpu())
+        host_in.append(h)
+    outs = _step_outputs(wl)
+    host_out = [torch.empty(o.numel(), dtype=torch.uint8, pin_memory=True) for o in outs]
+    h2d = sum(h.numel() for h in host_in)
+    d2h = sum(h.numel() for h in host_out)
+
+    def e2e_step():
+        for h, d in zip(host_in, dev_in):
+            d.copy_(h, non_blocking=True)
+        wl.run()
+        for h, o in zip(host_out, outs):
+            h.copy_(o, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ee.record(stream)
+    barrier()
+    t_wall1 = time.time()
+    t = torch.tensor([es.elapsed_time(ee)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    if rank == 0:
+        sampler.stop()
+    _native.raise_on_device_error()
+
+    if rank == 0:
+        hbm_peak, bf16_peak, peak_src = measured_peaks()
+        ms_per_step = total_ms / args.steps
+        avg_s = ms_per_step * 1e-3
+        value = wl.global_flops / avg_s / 1e12
+        e2e_value = wl.global_flops / (e2e_ms / e2e_steps * 1e-3) / 1e12
+        if wl.bound == "hbm":
+            achieved = wl.bytes / avg_s / 1e9
+            roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                    "frac": round(achieved / hbm_peak, 4),
+                    "peak_source": f"{peak_src} hbm_gbs (burst copy), kernel timed alone"}
+        else:
+            fp4_peak = 4.0 * bf16_peak
+            achieved = wl.flops / avg_s / 1e12
+            roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(fp4_peak, 1),
+                    "unit": "TFLOP/s", "frac": round(achieved / fp4_peak, 4),
+                    "peak_source": f"4 x {peak_src} bf16_tflops (dense fp4 rate = 4x bf16 on B200)"}
+        roof["traffic"] = profile_traffic(f"nvfp4_gemm_{args.config}")
+        roof["algorithmic_bytes_per_launch"] = wl.bytes
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": warm, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
+            "dtype": "e2m1 x ue4m3 (nvfp4) -> f32 accumulate -> f16",
+            "data": "synthetic (BASELINE generation: N(0,1) -> e4m3 per-16 scale -> e2m1, seeded)",
+            "config": {"workload": wl.desc, "l2": "flushed by a 256 MiB write before every step",
+                       "timing": "CUDA events around each call on the launching stream, max over ranks",
+                       "parallelism": f"{wl.scaling} x{world}"},
+            "roofline": roof,
+            "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "path": "pinned host -> device copies, custom_kernel, device -> host copy"},
+            "gpu_launches": wl.launches_per_step * (args.steps + e2e_steps),
+            "clocks": sampler.summary(t_wall0, t_wall1),
+        }
+        if world == 1:
+            line["cpu_baseline"] = cpu_baseline(args, wl)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- CPU side
+def _numpy_inputs(wl):
+    import torch
+    if wl.kind.startswith("dense"):
+        a, b, sfa, sfb = wl.data[:4]
+        return ("dense", a.view(torch.uint8).permute(2, 0, 1).contiguous().cpu().numpy(),
+                b.view(torch.uint8).permute(2, 0, 1).contiguous().cpu().numpy(),
+                sfa.view(torch.uint8).cpu().numpy(), sfb.view(torch.uint8).cpu().numpy())
+    abc, sf, _, _ = wl.data
+    groups = []
+    for (a, b, _), (sa, sb) in zip(abc, sf):
+        groups.append((a.view(torch.uint8)[:, :, 0].cpu().numpy(), b.view(torch.uint8)[:, :, 0].cpu().numpy(),
+                       sa.view(torch.uint8)[:, :, 0].cpu().numpy(), sb.view(torch.uint8)[:, :, 0].cpu().numpy()))
+    return ("grouped", groups)
+
+
+def cpu_baseline(args, wl, budget_s=None):
+    """Reference semantics on the host: e2m1/e4m3 decode + fp32 matmul + fp16 cast
+    (oracle/nvfp4_oracle.py), on a bounded sample of the same workload."""
+    import numpy as np
+    from oracle import nvfp4_oracle as orc
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([p.get("num_threads", 1) for p in threadpool_info()] or [1])
+    except Exception:
+        threads = os.cpu_count() or 1
+    budget = budget_s if budget_s is not None else args.cpu_seconds
+    item = _numpy_inputs(wl)
+    if item[0] == "dense":
+        _, a, b, sa, sb = item
+        m, n, kk = a.shape[1], b.shape[1], a.shape[2] * 2
+        rows = max(1, min(m, 64))
+        cols = max(1, min(n, 16384))
+        a_s, sa_s, b_s, sb_s = a[:, :rows], sa[:rows], b[:, :cols], sb[:cols]
+        flops_call = 2.0 * rows * cols * kk
+        run = lambda: orc.gemm_ref(a_s, b_s, sa_s, sb_s, dtype=np.float32)
+        sample = f"rows 0..{rows - 1} of A x columns 0..{cols - 1} of B, K={kk} (workload {m}x{n}x{kk})"
+    else:
+        groups = item[1]
+        take = groups[: max(1, min(len(groups), 2))]
+        flops_call = sum(2.0 * g[0].shape[0] * g[1].shape[0] * g[0].shape[1] * 2 for g in take)
+        run = lambda: orc.grouped_gemm_ref(take, dtype=np.float32)
+        sample = f"first {len(take)} of {len(groups)} groups"
+    t0 = time.perf_counter()
+    run()
+    one = time.perf_counter() - t0
+    reps = max(1, min(20, int(budget / max(one, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        run()
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(flops_call / dt / 1e12, 6), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{sample}; {reps} reps, {dt:.3f} s each "
+                      f"(numpy LUT decode, {threads}-thread OpenBLAS sgemm, fp16 cast)"}
+
+
+def bench_reference(args):
+    """Reference arm: the reference's path semantics on the host cores (rank 0 only)."""
+    import torch
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    w = WORKLOADS[args.config]
+    device = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    from nvfp4_hackathon_b200 import inputs
+
+    class _WL:
+        pass
+    wl = _WL()
+    if w["kind"].startswith("dense"):
+        wl.kind = "dense"
+        wl.data = inputs.generate_quantized_input(w["m"], w["n"], w["k"], 1, seed=1111, device=device)
+    else:
+        ms = inputs.uniform_group_sizes(w["g"], 1111) if w["kind"] == "grouped" else \
+            inputs.zipf_group_sizes(w["g"], w["tokens"])
+        wl.kind = "grouped"
+        wl.data = inputs.generate_quantized_group_input(ms, w["n"], w["k"], seed=1111, device=device)
+    cb = cpu_baseline(args, wl, budget_s=max(5.0, min(60.0, args.cpu_seconds)))
+    line = {"metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "impl": "reference", "scaling": "weak",
+            "vs_baseline": None, "dtype": "e2m1 x e4m3 decoded to f32, f32 matmul, f16",
+            "data": "synthetic (BASELINE generation)",
+            "config": {"workload": w["desc"],
+                       "note": "reference semantics (kernels/gemm/reference.py:27-53) restated for the host "
+                               "(oracle/nvfp4_oracle.py); the reference has no CPU implementation"},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        bench_reference(args)
+    else:
+        bench_ours(args)
+
+
+if __name__ == "__main__":
+    main()

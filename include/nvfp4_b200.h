@@ -109,6 +109,25 @@ int nvfp4_grouped_gemm_ex(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev
                           const uint64_t* sf_ptrs_dev, int G, void* workspace,
                           size_t workspace_bytes, void* stream, const nvfp4_options* opt);
 
+/*
+ * Grouped NVFP4 GEMM that allocates nothing.  No counterpart in the reference;
+ * it is for callers that must not allocate device memory at call time, such as
+ * code running inside a pre-planned memory pool or a host runtime that owns
+ * every allocation itself, and so cannot provide the workspace that
+ * nvfp4_grouped_gemm wants.  Same tables, same results as nvfp4_grouped_gemm
+ * with default options.
+ * Limit: 1 <= G <= 256 (larger G is rejected with NVFP4_ERR_UNSUPPORTED).
+ * The scratch (about 66 KiB for the per-group tensor maps and tile schedule) is
+ * a fixed device array inside the library; each GPU that loads the library
+ * holds it until the process exits.  The first call on a device looks up that
+ * array's address (with that device current); make that first call before any
+ * stream capture.  All calls on a device share the one array, so two calls
+ * that may run at the same time on the GPU (different streams, no ordering
+ * between them) race and give wrong results; calls on one stream are fine.
+ */
+int nvfp4_grouped_gemm_noalloc(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev,
+                               const uint64_t* sf_ptrs_dev, int G, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

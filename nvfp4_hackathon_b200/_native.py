@@ -43,6 +43,7 @@ EXPORTED = (
     "nvfp4_grouped_gemm_workspace_size",
     "nvfp4_grouped_gemm",
     "nvfp4_grouped_gemm_ex",
+    "nvfp4_grouped_gemm_noalloc",
 )
 
 
@@ -97,6 +98,7 @@ def load() -> ctypes.CDLL:
         lib.nvfp4_grouped_gemm.argtypes = [vp, vp, vp, i, vp, sz, vp]
         lib.nvfp4_grouped_gemm_ex.argtypes = [vp, vp, vp, i, vp, sz, vp,
                                               ctypes.POINTER(Nvfp4Options)]
+        lib.nvfp4_grouped_gemm_noalloc.argtypes = [vp, vp, vp, i, vp]
         for name in EXPORTED:
             getattr(lib, name)  # AttributeError here means a stale build
         _lib = lib

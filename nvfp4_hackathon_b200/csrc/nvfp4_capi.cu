@@ -435,3 +435,56 @@ int nvfp4_grouped_gemm(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev,
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ grouped GEMM without allocation
+// Scratch for nvfp4_grouped_gemm_noalloc: room for the per-group tensor maps and
+// the tile prefix of up to kNoAllocMaxGroups groups (about 66 KiB).  Every GPU
+// that loads the library holds one copy until the process exits.  In host code
+// the name below is only a host-side stand-in; the device address comes from
+// cudaGetSymbolAddress, once per device.
+constexpr int kNoAllocMaxGroups = 256;
+constexpr size_t kNoAllocScratchBytes =
+    ((size_t)kNoAllocMaxGroups * 2 * sizeof(CUtensorMap) + 255) / 256 * 256 +
+    ((size_t)(kNoAllocMaxGroups + 1) * 4 + 255) / 256 * 256;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+}  // namespace
+
+extern "C" int nvfp4_grouped_gemm_noalloc(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev,
+                                          const uint64_t* sf_ptrs_dev, int G, void* stream) {
+  if (G <= 0 || G > kNoAllocMaxGroups)
+    return fail(NVFP4_ERR_UNSUPPORTED,
+                "nvfp4_grouped_gemm_noalloc handles 1..%d groups (got %d); use nvfp4_grouped_gemm "
+                "with a caller-allocated workspace for more",
+                kNoAllocMaxGroups, G);
+  if (!sizes_dev || !abc_ptrs_dev || !sf_ptrs_dev)
+    return fail(NVFP4_ERR_INVALID_ARG, "null group table");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      // first call on this device (the current one): look up the array's device address
+      e = cudaGetSymbolAddress(&g_noalloc_ptr[dev], g_noalloc_scratch);
+      if (e != cudaSuccess) {
+        g_noalloc_ptr[dev] = nullptr;
+        return cuda_fail(e, "cudaGetSymbolAddress(grouped scratch)");
+      }
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  if (grouped_ws_bytes(G) > kNoAllocScratchBytes)
+    return fail(NVFP4_ERR_WORKSPACE, "internal: scratch too small for %d groups", G);
+  // The prep kernel rewrites the tile prefix and the maps of every non-empty
+  // group on each call, so nothing in the scratch has to start at zero.
+  return run_grouped_bn<kGroupedBN>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, scratch,
+                                    static_cast<cudaStream_t>(stream), st, nullptr);
+}

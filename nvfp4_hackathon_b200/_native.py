@@ -72,9 +72,13 @@ def lib_path() -> str:
 
 def load() -> ctypes.CDLL:
     """Load (once) and return the library; raises ImportError when it is absent."""
-    global _lib
     if _lib is not None:
         return _lib
+    return _load_slow()
+
+
+def _load_slow() -> ctypes.CDLL:
+    global _lib
     with _lock:
         if _lib is not None:
             return _lib

@@ -14,6 +14,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "nvfp4_kernels.cuh"
 #include "../../include/nvfp4_b200.h"
@@ -105,7 +106,67 @@ int encode_operand_map(CUtensorMap* m, const void* ptr, long long rows, long lon
   return NVFP4_OK;
 }
 
+// Per-thread memo of recent operand maps: a repeated call on the same buffers skips
+// the driver encode (about a microsecond each).  The key covers every input of the
+// encoding, so a hit is exactly the map the driver would build again.
+struct MapKey {
+  const void* ptr;
+  long long rows, kbytes, batch;
+  int box_rows;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && rows == o.rows && kbytes == o.kbytes && batch == o.batch &&
+           box_rows == o.box_rows;
+  }
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map;
+  bool valid;
+};
+constexpr int kMapCache = 16;
+thread_local MapEntry g_map_cache[kMapCache];
+thread_local int g_map_next = 0;
+
+int cached_operand_map(CUtensorMap* m, const void* ptr, long long rows, long long kbytes,
+                       long long batch, int box_rows) {
+  const MapKey key{ptr, rows, kbytes, batch, box_rows};
+  for (int i = 0; i < kMapCache; ++i)
+    if (g_map_cache[i].valid && g_map_cache[i].key == key) {
+      *m = g_map_cache[i].map;
+      return NVFP4_OK;
+    }
+  int rc = encode_operand_map(m, ptr, rows, kbytes, batch, box_rows);
+  if (rc) return rc;
+  MapEntry& e = g_map_cache[g_map_next];
+  g_map_next = (g_map_next + 1) % kMapCache;
+  e.key = key;
+  e.map = *m;
+  e.valid = true;
+  return NVFP4_OK;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launch with programmatic stream serialization: the kernel may start while the
+// previous kernel on the stream finishes; it calls griddepcontrol.wait before it
+// touches global memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e;
+}
 
 template <bool GROUPED, bool SWAP, int BN>
 int launch(const CUtensorMap& tp, const CUtensorMap& tq, const GemmParams& prm, int grid,
@@ -121,8 +182,7 @@ int launch(const CUtensorMap& tp, const CUtensorMap& tq, const GemmParams& prm, 
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     attr_done[dev] = true;
   }
-  kern<<<grid, kNumThreads, C_::kSmemBytes, stream>>>(tp, tq, prm);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kNumThreads), C_::kSmemBytes, stream, tp, tq, prm);
   if (e != cudaSuccess) return cuda_fail(e, "nvfp4_gemm_kernel launch");
   return NVFP4_OK;
 }
@@ -159,9 +219,9 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   const int q_rows = SWAP ? m : n;
   const long long kbytes = k / 2;
   CUtensorMap tp, tq;
-  int rc = encode_operand_map(&tp, P, p_rows, kbytes, l, kBM);
+  int rc = cached_operand_map(&tp, P, p_rows, kbytes, l, kBM);
   if (rc) return rc;
-  rc = encode_operand_map(&tq, Q, q_rows, kbytes, l, BN);
+  rc = cached_operand_map(&tq, Q, q_rows, kbytes, l, BN);
   if (rc) return rc;
   GemmParams prm;
   std::memset(&prm, 0, sizeof(prm));
@@ -233,6 +293,9 @@ nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_cons
                    const unsigned long long* __restrict__ sfs, int G, CUtensorMap* maps,
                    int* prefix, int bn, int* status) {
   __shared__ int warp_sums[kMaxGroups / 32];
+  pdl_launch_dependents();
+  // the workspace may still be read by the previous call's GEMM on this stream
+  pdl_wait_prior_grid();
   const int g = threadIdx.x;
   int tiles = 0;
   if (g < G) {
@@ -305,11 +368,10 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   int* prefix = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) +
                                        align_up((size_t)G * 2 * sizeof(CUtensorMap), 256));
   const int threads = ((G + 31) / 32) * 32;
-  nvfp4_grouped_prep<<<1, threads, 0, stream>>>(tp, tq, sizes,
-                                                reinterpret_cast<const unsigned long long*>(abc),
-                                                reinterpret_cast<const unsigned long long*>(sfs), G,
-                                                maps, prefix, BN, st->status);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(nvfp4_grouped_prep, dim3(1), dim3(threads), 0, stream, tp, tq, sizes,
+                             reinterpret_cast<const unsigned long long*>(abc),
+                             reinterpret_cast<const unsigned long long*>(sfs), G, maps, prefix, BN,
+                             st->status);
   if (e != cudaSuccess) return cuda_fail(e, "nvfp4_grouped_prep launch");
   GemmParams prm;
   std::memset(&prm, 0, sizeof(prm));

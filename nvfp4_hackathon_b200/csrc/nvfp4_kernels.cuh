@@ -234,6 +234,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -262,6 +263,10 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above touches only shared memory, TMEM and kernel parameters, so it
+  // overlaps the previous kernel on the stream; global memory is used only after
+  // that kernel has completed.
+  pdl_wait_prior_grid();
 
   const int total = GROUPED ? __ldg(prm.tile_prefix + prm.G) : prm.total_tiles;
   const uint64_t tmo = prm.timeout_ns;

@@ -9,6 +9,7 @@ tensors are ignored, as in the reference.
 from __future__ import annotations
 
 import ctypes
+import weakref
 
 import torch
 
@@ -17,6 +18,12 @@ from .layout import SF_VEC, ceil_div, is_permuted_layout
 from .task import gemm_input_t, gemm_output_t
 
 _compiled = None
+# Memo of validated argument sets: (weak refs to the 5 tensors, m, n, k, l).  A hit
+# needs the very same tensor objects (still alive), so only an in-place change of
+# their shape, strides or storage (resize_, set_, as_strided_) would bypass the
+# checks.  Bounded, and holds no strong references.
+_validated: dict = {}
+_VALIDATED_MAX = 32
 
 
 def compile_kernel():
@@ -39,6 +46,10 @@ def _check_operand(t: torch.Tensor, rows: int, kb: int, l: int, name: str) -> No
         raise ValueError(f"{name} must be K-major with batch outermost, strides {want}; got {t.stride()}")
 
 
+def _current_stream(t: torch.Tensor) -> int:
+    return torch._C._cuda_getCurrentRawStream(t.get_device())
+
+
 def launch(a, b, sfa_perm, sfb_perm, c, m: int, n: int, k: int, l: int, stream=None,
            opt: _native.Nvfp4Options | None = None) -> None:
     """Raw launch on device pointers (tensors or ints); no layout checks."""
@@ -53,8 +64,7 @@ def launch(a, b, sfa_perm, sfb_perm, c, m: int, n: int, k: int, l: int, stream=N
     _native.check(rc, "nvfp4_gemm")
 
 
-def custom_kernel(data: gemm_input_t, opt: _native.Nvfp4Options | None = None) -> gemm_output_t:
-    a, b, _, _, sfa_perm, sfb_perm, c = data
+def _validate(a, b, sfa_perm, sfb_perm, c):
     m, kb, l = a.shape
     n = b.shape[0]
     k = 2 * kb  # two e2m1 values per byte (submission.py:779)
@@ -67,5 +77,27 @@ def custom_kernel(data: gemm_input_t, opt: _native.Nvfp4Options | None = None) -
     sf_k = ceil_div(k, SF_VEC)
     if not is_permuted_layout(sfa_perm, m, sf_k, l) or not is_permuted_layout(sfb_perm, n, sf_k, l):
         raise ValueError("scale tensors must use the permuted (32, 4, rest_mn, 4, rest_k, l) layout")
-    launch(a, b, sfa_perm, sfb_perm, c, m, n, k, l, opt=opt)
+    return m, n, k, l
+
+
+def custom_kernel(data: gemm_input_t, opt: _native.Nvfp4Options | None = None) -> gemm_output_t:
+    a, b, _, _, sfa_perm, sfb_perm, c = data
+    key = (id(a), id(b), id(sfa_perm), id(sfb_perm), id(c))
+    hit = _validated.get(key)
+    if hit is not None and all(r() is t for r, t in zip(hit[0], (a, b, sfa_perm, sfb_perm, c))):
+        m, n, k, l = hit[1]
+    else:
+        m, n, k, l = _validate(a, b, sfa_perm, sfb_perm, c)
+        if len(_validated) >= _VALIDATED_MAX:
+            _validated.clear()
+        _validated[key] = (tuple(weakref.ref(t) for t in (a, b, sfa_perm, sfb_perm, c)), (m, n, k, l))
+    lib = _native.load()
+    if opt is None:
+        rc = lib.nvfp4_gemm(a.data_ptr(), b.data_ptr(), sfa_perm.data_ptr(), sfb_perm.data_ptr(),
+                            c.data_ptr(), m, n, k, l, _current_stream(a))
+    else:
+        rc = lib.nvfp4_gemm_ex(a.data_ptr(), b.data_ptr(), sfa_perm.data_ptr(), sfb_perm.data_ptr(),
+                               c.data_ptr(), m, n, k, l, _current_stream(a), ctypes.byref(opt))
+    if rc:
+        _native.check(rc, "nvfp4_gemm")
     return c

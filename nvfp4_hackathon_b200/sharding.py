@@ -92,7 +92,10 @@ def gather_columns(c_shard, gathered, dist) -> None:
         import torch
         src = torch.zeros((m, n_pad), dtype=c_shard.dtype, device=c_shard.device)
         src[:, :w] = c_shard
-    dist.all_gather_into_tensor(gathered, src)
+    if dist.get_backend() == "nccl":
+        dist.all_gather_into_tensor(gathered, src)  # one NCCL collective over NVLink
+    else:  # gloo (CPU tests) has no all_gather_into_tensor
+        dist.all_gather(list(gathered.unbind(0)), src)
 
 
 def assemble_columns(gathered, n: int, world: int):

@@ -12,15 +12,15 @@
 // "swap" P = B, Q = A and C[m, n] = D[n, m], which puts a skinny M (decode-like
 // shapes, small MoE groups) on the flexible N side of the MMA.
 //
-// Roles (18 warps):
+// Roles (19 warps):
 //   warps 0-7   epilogue: warp w drains TMEM lanes 32*(w%4).. and column half w/4 of the
 //               accumulator into registers as fp16, releases the accumulator, then stores
 //               to global while the next tile's MMAs already run
-//   warp 8      producer: TMA loads of the P and Q tiles (128-byte swizzle) and plain bulk
-//               copies of the scale atoms into a ring of kStages shared-memory stages
-//   warp 9      TMEM owner and MMA issuer: tcgen05.mma kind::mxf4nvf4 (K = 64 per
+//   warps 8-9   producers (alternating k-stages): TMA loads of the P and Q tiles (128-byte
+//               swizzle) and plain bulk copies of the scale atoms into a ring of kStages stages
+//   warp 10     TMEM owner and MMA issuer: tcgen05.mma kind::mxf4nvf4 (K = 64 per
 //               instruction), one tcgen05.commit per stage to release it.
-//   warps 10-17 scale warps, two groups of four (group g serves stages with s % 2 == g):
+//   warps 11-18 scale warps, two groups of four (group g serves stages with s % 2 == g):
 //               each warp moves the stage's scale atoms from shared memory into its own 32
 //               TMEM lanes with ld.shared + tcgen05.st.  (tcgen05.cp costs ~115 cycles per
 //               512-byte atom on the copy engine; register stores run alongside the MMAs.)
@@ -48,9 +48,10 @@ constexpr int kBKBytes = 128;       // bytes of K per stage (256 fp4 values)
 constexpr int kBK = 256;            // K elements per stage
 constexpr int kAtomBytes = 512;     // one scale-factor atom: 128 rows x 4 K-vectors
 constexpr int kEpiWarps = 8;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kFirstSfWarp = 10;
+constexpr int kProducerWarp = 8;   // warps 8 and 9: stage issue alternates between them
+constexpr int kNumProducers = 2;
+constexpr int kMmaWarp = 10;
+constexpr int kFirstSfWarp = 11;
 constexpr int kSfGroups = 2;        // groups of 4 scale warps; group g serves stages s % 2 == g
 constexpr int kNumThreads = 32 * (kFirstSfWarp + 4 * kSfGroups);
 constexpr int kSmemBudget = 232448 - 2048;  // dynamic smem per CTA minus alignment/barriers
@@ -251,7 +252,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     fence_mbar_init();
     fence_async_shared();
   }
-  if (warp == kProducerWarp && lane == 0 && !GROUPED) {
+  if (warp >= kProducerWarp && warp < kProducerWarp + kNumProducers && lane == 0 && !GROUPED) {
     prefetch_tmap(&tm_p);
     prefetch_tmap(&tm_q);
   }
@@ -283,9 +284,13 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     return kbv > 4 ? 4 : kbv;
   };
 
-  if (warp == kProducerWarp) {
+  if (warp >= kProducerWarp && warp < kProducerWarp + kNumProducers) {
     if (lane == 0 && !(prm.debug & 1)) {
-      // ------------------------------------------------------------ producer
+      // ------------------------------------------------------------ producers
+      // Producer j issues the loads of k-steps j, j + 2, ...: one thread issuing TMA and
+      // bulk copies tops out at about one 28 KB stage per ~250 ns, two double that.
+      const uint32_t pid = warp - kProducerWarp;
+      uint32_t gstep = 0;
       const uint64_t pol_keep = policy_evict_last();
       int s = 0;
       uint32_t ph = 0;
@@ -304,7 +309,11 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         const int pblk = ti.p0 >> 7;
         const int qblk = ti.q0 >> 7;
         const int nq_atoms = q_atoms(ti);
-        for (int kt = 0; kt < ti.num_kt; ++kt) {
+        for (int kt = 0; kt < ti.num_kt; ++kt, ++gstep) {
+          if ((gstep & 1) != pid) {  // the other producer's step (S is even: stage parity == step parity)
+            if (++s == S) { s = 0; ph ^= 1; }
+            continue;
+          }
           if (!mbar_wait_bounded(empty_bar(s), ph ^ 1, abort_flag, prm.status,
                                  kStatusTimeoutProducer, tmo)) { ok = false; break; }
           if (prm.debug & 2) {  // timing probe: no data movement
@@ -324,7 +333,8 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
             bulk_load(st + kOffSfq + a * 4 * kAtomBytes,
                       ti.sf_q + ((long long)(qblk + a) * ti.rk + kt * 4) * kAtomBytes, sf_bytes,
                       full_bar(s), pol_keep);
-          trace_event(prm, 0, pstep++);
+          if (pid == 0) trace_event(prm, 0, pstep);
+          pstep += 1;
           issued_mask |= 1u << s;
           issued_par = (issued_par & ~(1u << s)) | (ph << s);
           if (++s == S) { s = 0; ph ^= 1; }

@@ -55,6 +55,8 @@ class Nvfp4Options(ctypes.Structure):
         ("timeout_ns", ctypes.c_ulonglong),
         ("debug", ctypes.c_int),
         ("trace", ctypes.c_void_p),
+        ("stage_k", ctypes.c_int),
+        ("cta_pair", ctypes.c_int),
     ]
 
 
@@ -133,5 +135,6 @@ def raise_on_device_error() -> None:
         raise Nvfp4Error(f"device-side error: {STATUS.get(s, s)}")
 
 
-def options(operand_order=0, tile_n=0, max_ctas=0, timeout_ns=0, debug=0, trace=None):
-    return Nvfp4Options(operand_order, tile_n, max_ctas, timeout_ns, debug, trace)
+def options(operand_order=0, tile_n=0, max_ctas=0, timeout_ns=0, debug=0, trace=None, stage_k=0,
+            cta_pair=0):
+    return Nvfp4Options(operand_order, tile_n, max_ctas, timeout_ns, debug, trace, stage_k, cta_pair)

@@ -89,16 +89,18 @@ int device_state(DeviceState** out) {
   return NVFP4_OK;
 }
 
-// Operand map: a (rows x kbytes x batch) uint8 tensor, K-major, 128-byte swizzle,
-// box = 128 bytes of K x box_rows rows.  Out-of-range rows read as zero.
+// Operand map: a (rows x kbytes x batch) uint8 tensor, K-major, box = box_inner bytes of
+// K (128 -> 128-byte swizzle, 64 -> 64-byte swizzle) x box_rows rows.  Out-of-range rows
+// read as zero.
 int encode_operand_map(CUtensorMap* m, const void* ptr, long long rows, long long kbytes,
-                       long long batch, int box_rows) {
+                       long long batch, int box_rows, int box_inner = 128) {
   cuuint64_t dims[3] = {(cuuint64_t)kbytes, (cuuint64_t)rows, (cuuint64_t)batch};
   cuuint64_t strides[2] = {(cuuint64_t)kbytes, (cuuint64_t)(rows * kbytes)};
-  cuuint32_t box[3] = {128u, (cuuint32_t)box_rows, 1u};
+  cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), dims, strides,
-                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        box_inner == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(NVFP4_ERR_DRIVER, "cuTensorMapEncodeTiled failed (%d) rows=%lld kbytes=%lld", (int)r,
@@ -112,10 +114,10 @@ int encode_operand_map(CUtensorMap* m, const void* ptr, long long rows, long lon
 struct MapKey {
   const void* ptr;
   long long rows, kbytes, batch;
-  int box_rows;
+  int box_rows, box_inner;
   bool operator==(const MapKey& o) const {
     return ptr == o.ptr && rows == o.rows && kbytes == o.kbytes && batch == o.batch &&
-           box_rows == o.box_rows;
+           box_rows == o.box_rows && box_inner == o.box_inner;
   }
 };
 struct MapEntry {
@@ -128,14 +130,14 @@ thread_local MapEntry g_map_cache[kMapCache];
 thread_local int g_map_next = 0;
 
 int cached_operand_map(CUtensorMap* m, const void* ptr, long long rows, long long kbytes,
-                       long long batch, int box_rows) {
-  const MapKey key{ptr, rows, kbytes, batch, box_rows};
+                       long long batch, int box_rows, int box_inner) {
+  const MapKey key{ptr, rows, kbytes, batch, box_rows, box_inner};
   for (int i = 0; i < kMapCache; ++i)
     if (g_map_cache[i].valid && g_map_cache[i].key == key) {
       *m = g_map_cache[i].map;
       return NVFP4_OK;
     }
-  int rc = encode_operand_map(m, ptr, rows, kbytes, batch, box_rows);
+  int rc = encode_operand_map(m, ptr, rows, kbytes, batch, box_rows, box_inner);
   if (rc) return rc;
   MapEntry& e = g_map_cache[g_map_next];
   g_map_next = (g_map_next + 1) % kMapCache;
@@ -152,27 +154,35 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // touches global memory.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                       Args&&... args) {
+                       int cluster, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    n = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = n;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
   if (e == cudaSuccess) e = cudaGetLastError();
   return e;
 }
 
-template <bool GROUPED, bool SWAP, int BN>
+template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false>
 int launch(const CUtensorMap& tp, const CUtensorMap& tq, const GemmParams& prm, int grid,
            cudaStream_t stream) {
-  using C_ = Cfg<BN>;
-  auto kern = nvfp4_gemm_kernel<GROUPED, SWAP, BN>;
+  using C_ = Cfg<BN, KB, CTA2>;
+  auto kern = nvfp4_gemm_kernel<GROUPED, SWAP, BN, KB, CTA2>;
   static bool attr_done[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -182,7 +192,8 @@ int launch(const CUtensorMap& tp, const CUtensorMap& tq, const GemmParams& prm, 
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     attr_done[dev] = true;
   }
-  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kNumThreads), C_::kSmemBytes, stream, tp, tq, prm);
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kNumThreads), C_::kSmemBytes, stream,
+                             CTA2 ? 2 : 1, tp, tq, prm);
   if (e != cudaSuccess) return cuda_fail(e, "nvfp4_gemm_kernel launch");
   return NVFP4_OK;
 }
@@ -190,15 +201,21 @@ int launch(const CUtensorMap& tp, const CUtensorMap& tq, const GemmParams& prm, 
 struct DenseChoice {
   bool swap;
   int bn;
+  int kb;    // 64-wide K blocks per stage (2 or 4)
+  bool cta2; // M = 256 tiles over a CTA pair (tcgen05 cta_group::2)
 };
 
 DenseChoice choose_dense(int m, int n, int k, const nvfp4_options* opt) {
   (void)k;
   DenseChoice c;
-  if (m <= 64) c = {true, 64};
-  else if (m <= 128) c = {true, 128};
-  else c = {false, (n >= 2048) ? 256 : 128};
+  if (m <= 64) c = {true, 64, 4, false};
+  else if (m <= 128) c = {true, 128, 4, false};
+  else c = {false, (n >= 2048) ? 256 : 128, 4, false};
   if (opt) {
+    if (opt->cta_pair == 1) c.cta2 = false;
+    if (opt->cta_pair == 2) c.cta2 = true;
+    if (opt->stage_k == 128) c.kb = 2;
+    if (opt->stage_k == 256) c.kb = 4;
     if (opt->operand_order == 1) c.swap = false;
     if (opt->operand_order == 2) c.swap = true;
     if (opt->tile_n > 0) c.bn = opt->tile_n;
@@ -206,7 +223,7 @@ DenseChoice choose_dense(int m, int n, int k, const nvfp4_options* opt) {
   return c;
 }
 
-template <bool SWAP, int BN>
+template <bool SWAP, int BN, int KB, bool CTA2 = false>
 int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb, void* c, int m,
                  int n, int k, int l, cudaStream_t stream, DeviceState* st,
                  const nvfp4_options* opt) {
@@ -219,9 +236,9 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   const int q_rows = SWAP ? m : n;
   const long long kbytes = k / 2;
   CUtensorMap tp, tq;
-  int rc = cached_operand_map(&tp, P, p_rows, kbytes, l, kBM);
+  int rc = cached_operand_map(&tp, P, p_rows, kbytes, l, kBM, KB * 32);
   if (rc) return rc;
-  rc = cached_operand_map(&tq, Q, q_rows, kbytes, l, BN);
+  rc = cached_operand_map(&tq, Q, q_rows, kbytes, l, CTA2 ? BN / 2 : BN, KB * 32);
   if (rc) return rc;
   GemmParams prm;
   std::memset(&prm, 0, sizeof(prm));
@@ -237,7 +254,8 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   prm.C = static_cast<__half*>(c);
   prm.ldc = n;
   prm.c_batch = (long long)m * n;
-  prm.tiles_p = (p_rows + kBM - 1) / kBM;
+  const int pm = CTA2 ? 2 * kBM : kBM;  // P rows per tile (a CTA pair covers 256)
+  prm.tiles_p = (p_rows + pm - 1) / pm;
   prm.tiles_q = (q_rows + BN - 1) / BN;
   const long long total = (long long)prm.tiles_p * prm.tiles_q * l;
   if (total > 0x7fffffffLL) return fail(NVFP4_ERR_UNSUPPORTED, "too many tiles");
@@ -249,8 +267,15 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   prm.trace = opt ? reinterpret_cast<unsigned long long*>(opt->trace) : nullptr;
   int grid = st->num_sms;
   if (opt && opt->max_ctas > 0 && opt->max_ctas < grid) grid = opt->max_ctas;
-  if (grid > prm.total_tiles) grid = prm.total_tiles;
-  return launch<false, SWAP, BN>(tp, tq, prm, grid, stream);
+  if (CTA2) {
+    int pairs = grid / 2;
+    if (pairs > prm.total_tiles) pairs = prm.total_tiles;
+    if (pairs < 1) pairs = 1;
+    grid = 2 * pairs;
+  } else if (grid > prm.total_tiles) {
+    grid = prm.total_tiles;
+  }
+  return launch<false, SWAP, BN, KB, CTA2>(tp, tq, prm, grid, stream);
 }
 
 // ------------------------------------------------------------------ grouped GEMM
@@ -354,21 +379,21 @@ nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_cons
   if (g == 0) prefix[0] = 0;
 }
 
-template <int BN>
+template <int BN, int KB = 4>
 int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sfs, int G, void* ws,
                    cudaStream_t stream, DeviceState* st, const nvfp4_options* opt) {
   // Templates: any valid 16-byte-aligned address and sizes; the prep kernel
   // replaces address, extents and strides per group.
   CUtensorMap tp, tq;
-  int rc = encode_operand_map(&tp, ws, 128, 128, 1, kBM);
+  int rc = encode_operand_map(&tp, ws, 128, 128, 1, kBM, KB * 32);
   if (rc) return rc;
-  rc = encode_operand_map(&tq, ws, 128, 128, 1, BN);
+  rc = encode_operand_map(&tq, ws, 128, 128, 1, BN, KB * 32);
   if (rc) return rc;
   CUtensorMap* maps = static_cast<CUtensorMap*>(ws);
   int* prefix = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) +
                                        align_up((size_t)G * 2 * sizeof(CUtensorMap), 256));
   const int threads = ((G + 31) / 32) * 32;
-  cudaError_t e = launch_pdl(nvfp4_grouped_prep, dim3(1), dim3(threads), 0, stream, tp, tq, sizes,
+  cudaError_t e = launch_pdl(nvfp4_grouped_prep, dim3(1), dim3(threads), 0, stream, 1, tp, tq, sizes,
                              reinterpret_cast<const unsigned long long*>(abc),
                              reinterpret_cast<const unsigned long long*>(sfs), G, maps, prefix, BN,
                              st->status);
@@ -387,7 +412,7 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   prm.trace = opt ? reinterpret_cast<unsigned long long*>(opt->trace) : nullptr;
   int grid = st->num_sms;
   if (opt && opt->max_ctas > 0 && opt->max_ctas < grid) grid = opt->max_ctas;
-  return launch<true, true, BN>(tp, tq, prm, grid, stream);
+  return launch<true, true, BN, KB>(tp, tq, prm, grid, stream);
 }
 
 }  // namespace
@@ -442,17 +467,31 @@ int nvfp4_gemm_ex(const void* a, const void* b, const void* sfa_perm, const void
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   DenseChoice ch = choose_dense(m, n, k, opt);
-#define NVFP4_DENSE_CASE(SW, BNV)                                                         \
-  if (ch.swap == SW && ch.bn == BNV)                                                      \
-    return run_dense_bn<SW, BNV>(a, b, sfa_perm, sfb_perm, c, m, n, k, l, s, st, opt);
-  NVFP4_DENSE_CASE(true, 64)
-  NVFP4_DENSE_CASE(true, 128)
-  NVFP4_DENSE_CASE(true, 256)
-  NVFP4_DENSE_CASE(false, 64)
-  NVFP4_DENSE_CASE(false, 128)
-  NVFP4_DENSE_CASE(false, 256)
+#define NVFP4_DENSE_CASE(SW, BNV, KBV)                                                    \
+  if (!ch.cta2 && ch.swap == SW && ch.bn == BNV && ch.kb == KBV)                                      \
+    return run_dense_bn<SW, BNV, KBV>(a, b, sfa_perm, sfb_perm, c, m, n, k, l, s, st, opt);
+  NVFP4_DENSE_CASE(true, 64, 4)
+  NVFP4_DENSE_CASE(true, 128, 4)
+  NVFP4_DENSE_CASE(true, 256, 4)
+  NVFP4_DENSE_CASE(false, 64, 4)
+  NVFP4_DENSE_CASE(false, 128, 4)
+  NVFP4_DENSE_CASE(false, 256, 4)
+  NVFP4_DENSE_CASE(true, 64, 2)
+  NVFP4_DENSE_CASE(true, 128, 2)
+  NVFP4_DENSE_CASE(false, 128, 2)
+  NVFP4_DENSE_CASE(false, 256, 2)
 #undef NVFP4_DENSE_CASE
-  return fail(NVFP4_ERR_UNSUPPORTED, "no kernel for swap=%d tile_n=%d", (int)ch.swap, ch.bn);
+#define NVFP4_PAIR_CASE(SW, BNV)                                                              \
+  if (ch.cta2 && ch.swap == SW && ch.bn == BNV && ch.kb == 4)                                   \
+    return run_dense_bn<SW, BNV, 4, true>(a, b, sfa_perm, sfb_perm, c, m, n, k, l, s, st, opt);
+  NVFP4_PAIR_CASE(true, 64)
+  NVFP4_PAIR_CASE(true, 128)
+  NVFP4_PAIR_CASE(false, 128)
+  NVFP4_PAIR_CASE(false, 256)
+#undef NVFP4_PAIR_CASE
+#undef NVFP4_DENSE_CASE
+  return fail(NVFP4_ERR_UNSUPPORTED, "no kernel for swap=%d tile_n=%d stage_k=%d", (int)ch.swap, ch.bn,
+              ch.kb * 64);
 }
 
 int nvfp4_gemm(const void* a, const void* b, const void* sfa_perm, const void* sfb_perm, void* c,
@@ -483,7 +522,10 @@ int nvfp4_grouped_gemm_ex(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev
   const int bn = (opt && opt->tile_n > 0) ? opt->tile_n : kGroupedBN;
   switch (bn) {
     case 64: return run_grouped_bn<64>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
-    case 128: return run_grouped_bn<128>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
+    case 128:
+      if (opt && opt->stage_k == 128)
+        return run_grouped_bn<128, 2>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
+      return run_grouped_bn<128>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
     case 256: return run_grouped_bn<256>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
     default: return fail(NVFP4_ERR_UNSUPPORTED, "grouped tile_n %d not built", bn);
   }

@@ -20,7 +20,7 @@
 //               swizzle) and plain bulk copies of the scale atoms into a ring of kStages stages
 //   warp 10     TMEM owner and MMA issuer: tcgen05.mma kind::mxf4nvf4 (K = 64 per
 //               instruction), one tcgen05.commit per stage to release it.
-//   warps 11-18 scale warps, two groups of four (group g serves stages with s % 2 == g):
+//   warps 11-18 scale warps, two groups of four (group g serves k-step pairs j with j % 2 == g):
 //               each warp moves the stage's scale atoms from shared memory into its own 32
 //               TMEM lanes with ld.shared + tcgen05.st.  (tcgen05.cp costs ~115 cycles per
 //               512-byte atom on the copy engine; register stores run alongside the MMAs.)
@@ -44,46 +44,58 @@
 namespace nvfp4 {
 
 constexpr int kBM = 128;            // MMA M (rows of P per tile)
-constexpr int kBKBytes = 128;       // bytes of K per stage (256 fp4 values)
-constexpr int kBK = 256;            // K elements per stage
 constexpr int kAtomBytes = 512;     // one scale-factor atom: 128 rows x 4 K-vectors
 constexpr int kEpiWarps = 8;
 constexpr int kProducerWarp = 8;   // warps 8 and 9: stage issue alternates between them
 constexpr int kNumProducers = 2;
 constexpr int kMmaWarp = 10;
 constexpr int kFirstSfWarp = 11;
-constexpr int kSfGroups = 2;        // groups of 4 scale warps; group g serves stages s % 2 == g
+constexpr int kSfGroups = 2;        // groups of 4 scale warps; group g serves k-step pairs j % 2 == g
 constexpr int kNumThreads = 32 * (kFirstSfWarp + 4 * kSfGroups);
 constexpr int kSmemBudget = 232448 - 2048;  // dynamic smem per CTA minus alignment/barriers
 
-template <int BN>
+// KB = 64-wide K blocks per pipeline stage: 4 (256 K, one 128-byte swizzle row per
+// operand row) or 2 (128 K, 64-byte swizzle).  Smaller stages fit twice as many in
+// shared memory, so stages are released and refilled at half the granularity.
+template <int BN, int KB, bool CTA2 = false>
 struct Cfg {
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
+  static_assert(KB == 2 || KB == 4, "KB must be 2 or 4");
+  static constexpr int kBKBytes = KB * 32;            // bytes of K per stage per row
+  static constexpr int kBK = KB * 64;                 // K elements per stage
+  static constexpr uint32_t kSwizzle = KB == 4 ? 2 : 4;  // smem descriptor: 128B / 64B swizzle
+  static constexpr uint32_t kSbo = 8 * kBKBytes;      // bytes between 8-row core-matrix groups
   static constexpr int kPBytes = kBM * kBKBytes;
-  static constexpr int kQBytes = BN * kBKBytes;
+  static constexpr int kQRows = CTA2 ? BN / 2 : BN;  // Q rows this CTA stages (the pair splits N)
+  static constexpr int kQBytes = kQRows * kBKBytes;
   static constexpr int kSfqAtoms = (BN <= 128) ? 1 : 2;  // 128-row scale blocks per Q tile
-  static constexpr int kSfpBytes = 4 * kAtomBytes;
-  static constexpr int kSfqBytes = kSfqAtoms * 4 * kAtomBytes;
+  static constexpr int kSfpBytes = KB * kAtomBytes;
+  static constexpr int kSfqBytes = kSfqAtoms * KB * kAtomBytes;
   static constexpr int kStageBytes = kPBytes + kQBytes + kSfpBytes + kSfqBytes;
   static constexpr int kSfqColsPerKb = 4 * kSfqAtoms;
-  // TMEM columns of one scale buffer: [SFP kb0..kb3 (16 columns)][SFQ kb0..kb3]
-  static constexpr int kSfCols = 16 + 4 * kSfqColsPerKb;
+  // TMEM columns of one scale buffer: [SFP kb0..kb(KB-1) (4 columns each)][SFQ kb0..]
+  static constexpr int kSfpCols = 4 * KB;
+  static constexpr int kSfCols = kSfpCols + KB * kSfqColsPerKb;
   static constexpr int kAccStages = (BN <= 128) ? 2 : 1;
   // one scale buffer per stage; stages come in pairs released by one commit
   static constexpr int kStagesSmem = kSmemBudget / kStageBytes;
   static constexpr int kStagesTmem = (512 - kAccStages * BN) / kSfCols;
   static constexpr int kStagesRaw = kStagesSmem < kStagesTmem ? kStagesSmem : kStagesTmem;
   static constexpr int kStagesCap = kStagesRaw > 8 ? 8 : kStagesRaw;
-  static constexpr int kStages = kStagesCap & ~1;  // even: the two scale-warp groups alternate
+  static constexpr int kStages = kStagesCap;
+  // scale hand-off barriers: pair j of consecutive k-steps uses sf_full[j % kPairBars];
+  // kPairBars >= (kStages + 1) / 2 + 1 keeps a barrier from being re-armed for pair
+  // j + kPairBars before the MMA issuer consumed pair j (those stages must be refilled first)
+  static constexpr int kPairBars = kStages / 2 + 1;
   static constexpr int kColsNeeded = kAccStages * BN + kStages * kSfCols;
   static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64
                                  : kColsNeeded <= 128 ? 128 : kColsNeeded <= 256 ? 256 : 512;
   static constexpr int kSfCol0 = kAccStages * BN;
   // barriers: full[S], sf_full[S/2], empty[S], acc_full[A], acc_empty[A], drain
-  static constexpr int kNumBars = 2 * kStages + kStages / 2 + 2 * kAccStages + 1;
+  static constexpr int kNumBars = 2 * kStages + kPairBars + 2 * kAccStages + 1;
   static constexpr int kBarrierBytes = 8 * kNumBars + 16;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
-  static_assert(kStages >= 2 && kStages % 2 == 0, "need an even number of stages");
+  static_assert(kStages >= 2, "need at least two stages");
   static_assert(kColsNeeded <= 512, "TMEM budget exceeded");
 };
 
@@ -142,10 +154,10 @@ struct TileInfo {
   __half* C;             // batch-adjusted base
   long long ldc;
   int rk;                // 64-wide K blocks (atoms per 128-row block)
-  int num_kt;            // 256-wide K stages
+  int num_kt;            // K stages (KB * 64 wide)
 };
 
-template <bool GROUPED, bool SWAP, int BN>
+template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false>
 __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtensorMap* tm_p,
                                             const CUtensorMap* tm_q, int t, TileInfo& ti) {
   if constexpr (!GROUPED) {
@@ -155,7 +167,8 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtenso
     int pb, qb;
     if (prm.q_fastest) { qb = r % prm.tiles_q; pb = r / prm.tiles_q; }
     else               { pb = r % prm.tiles_p; qb = r / prm.tiles_p; }
-    ti.p0 = pb * kBM;
+    // a CTA pair covers 256 P rows; this CTA owns rows [p0, p0 + 128)
+    ti.p0 = CTA2 ? pb * 2 * kBM + (int)cluster_ctarank() * kBM : pb * kBM;
     ti.q0 = qb * BN;
     ti.l = l;
     ti.p_rows = prm.p_rows;
@@ -168,7 +181,7 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtenso
     ti.C = prm.C + (long long)l * prm.c_batch;
     ti.ldc = prm.ldc;
     ti.rk = (prm.K + 63) / 64;
-    ti.num_kt = (prm.K + kBK - 1) / kBK;
+    ti.num_kt = (prm.K + KB * 64 - 1) / (KB * 64);
     return true;
   } else {
     // binary search the group whose tile range holds t
@@ -199,16 +212,17 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtenso
     ti.C = reinterpret_cast<__half*>(__ldg(prm.abc + 3 * g + 2));
     ti.ldc = n;
     ti.rk = (k + 63) / 64;
-    ti.num_kt = (k + kBK - 1) / kBK;
+    ti.num_kt = (k + KB * 64 - 1) / (KB * 64);
     return true;
   }
 }
 
-template <bool GROUPED, bool SWAP, int BN>
+template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
 nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constant__ CUtensorMap tm_q,
                   const GemmParams prm) {
-  using C_ = Cfg<BN>;
+  static_assert(!(CTA2 && GROUPED), "CTA pairs are used for the dense GEMM only");
+  using C_ = Cfg<BN, KB, CTA2>;
   constexpr int S = C_::kStages;
   constexpr int A = C_::kAccStages;
 
@@ -224,11 +238,12 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   constexpr uint32_t kOffSfq = kOffSfp + C_::kSfpBytes;
   const uint32_t bar_base = base + S * C_::kStageBytes;
   auto full_bar = [&](int s) { return bar_base + 8 * s; };
-  auto sff_bar = [&](int s) { return bar_base + 8 * (S + (s >> 1)); };  // one per stage pair
-  auto empty_bar = [&](int s) { return bar_base + 8 * (S + S / 2 + s); };
-  auto accf_bar = [&](int a) { return bar_base + 8 * (2 * S + S / 2 + a); };
-  auto acce_bar = [&](int a) { return bar_base + 8 * (2 * S + S / 2 + A + a); };
-  const uint32_t drain_bar = bar_base + 8 * (2 * S + S / 2 + 2 * A);
+  constexpr int P = C_::kPairBars;
+  auto sff_bar = [&](uint32_t pair) { return bar_base + 8 * (S + pair % P); };  // per k-step pair
+  auto empty_bar = [&](int s) { return bar_base + 8 * (S + P + s); };
+  auto accf_bar = [&](int a) { return bar_base + 8 * (2 * S + P + a); };
+  auto acce_bar = [&](int a) { return bar_base + 8 * (2 * S + P + A + a); };
+  const uint32_t drain_bar = bar_base + 8 * (2 * S + P + 2 * A);
   uint8_t* bar_ptr = smem + S * C_::kStageBytes;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bar_ptr + 8 * C_::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + 8 * C_::kNumBars + 4);
@@ -236,16 +251,27 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   pdl_launch_dependents();
+  // CTA pairs: rank 0 (leader) issues the MMAs for both; tiles are walked per pair.
+  const uint32_t crank = CTA2 ? cluster_ctarank() : 0;
+  const bool leader = crank == 0;
+  const int work0 = CTA2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int work_step = CTA2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  // arrive on the leader CTA's copy of a barrier (the pair's scale and accumulator hand-offs)
+  auto arrive_leader = [&](uint32_t bar) {
+    if (CTA2) mbar_arrive_cluster(mapa_shared(bar, 0));
+    else mbar_arrive(bar);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
-    for (int s = 0; s < S; s += 2) mbar_init(sff_bar(s), 4);  // one arrive per scale warp
+    // one arrive per scale warp (of both CTAs of a pair), one per epilogue warp
+    for (int b = 0; b < P; ++b) mbar_init(sff_bar(b), CTA2 ? 8 : 4);
     for (int a = 0; a < A; ++a) {
       mbar_init(accf_bar(a), 1);
-      mbar_init(acce_bar(a), 32 * kEpiWarps);
+      mbar_init(acce_bar(a), kEpiWarps * (CTA2 ? 2 : 1));
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -257,11 +283,17 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     prefetch_tmap(&tm_q);
   }
   if (warp == kMmaWarp) {
-    tmem_alloc(smem_u32(const_cast<uint32_t*>(tmem_slot)), C_::kTmemCols);
-    tmem_relinquish();
+    if (CTA2) {
+      tmem_alloc_2cta(smem_u32(const_cast<uint32_t*>(tmem_slot)), C_::kTmemCols);
+      tmem_relinquish_2cta();
+    } else {
+      tmem_alloc(smem_u32(const_cast<uint32_t*>(tmem_slot)), C_::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (CTA2) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // Everything above touches only shared memory, TMEM and kernel parameters, so it
@@ -280,8 +312,8 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     return nq;
   };
   auto k_blocks = [&](const TileInfo& ti, int kt) {
-    const int kbv = ti.rk - kt * 4;
-    return kbv > 4 ? 4 : kbv;
+    const int kbv = ti.rk - kt * KB;
+    return kbv > KB ? KB : kbv;
   };
 
   if (warp >= kProducerWarp && warp < kProducerWarp + kNumProducers) {
@@ -298,9 +330,9 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       bool ok = true;
       uint32_t issued_mask = 0, issued_par = 0;
       uint32_t pstep = 0;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      for (int t = work0; t < total && ok; t += work_step) {
         TileInfo ti;
-        decode_tile<GROUPED, SWAP, BN>(prm, &tm_p, &tm_q, t, ti);
+        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, t, ti);
         if (GROUPED && ti.map_p != last_map) {
           tmap_fence_acquire(ti.map_p);
           tmap_fence_acquire(ti.map_q);
@@ -325,13 +357,14 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           const uint32_t bytes = C_::kPBytes + C_::kQBytes + sf_bytes * (1 + nq_atoms);
           const uint32_t st = base + stage_off(s);
           mbar_arrive_expect_tx(full_bar(s), bytes);
-          tma_load_3d(st, ti.map_p, full_bar(s), kt * kBKBytes, ti.p0, ti.l, pol_keep);
-          tma_load_3d(st + kOffQ, ti.map_q, full_bar(s), kt * kBKBytes, ti.q0, ti.l, pol_keep);
-          bulk_load(st + kOffSfp, ti.sf_p + ((long long)pblk * ti.rk + kt * 4) * kAtomBytes,
+          tma_load_3d(st, ti.map_p, full_bar(s), kt * C_::kBKBytes, ti.p0, ti.l, pol_keep);
+          tma_load_3d(st + kOffQ, ti.map_q, full_bar(s), kt * C_::kBKBytes,
+                      ti.q0 + (int)crank * C_::kQRows, ti.l, pol_keep);
+          bulk_load(st + kOffSfp, ti.sf_p + ((long long)pblk * ti.rk + kt * KB) * kAtomBytes,
                     sf_bytes, full_bar(s), pol_keep);
           for (int a = 0; a < nq_atoms; ++a)
-            bulk_load(st + kOffSfq + a * 4 * kAtomBytes,
-                      ti.sf_q + ((long long)(qblk + a) * ti.rk + kt * 4) * kAtomBytes, sf_bytes,
+            bulk_load(st + kOffSfq + a * KB * kAtomBytes,
+                      ti.sf_q + ((long long)(qblk + a) * ti.rk + kt * KB) * kAtomBytes, sf_bytes,
                       full_bar(s), pol_keep);
           if (pid == 0) trace_event(prm, 0, pstep);
           pstep += 1;
@@ -348,7 +381,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       }
     }
   } else if (warp == kMmaWarp) {
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       // ------------------------------------------------------------ MMA issuer
       bool ok = true;
       int acc = 0;
@@ -356,25 +389,34 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       int s = 0;
       uint32_t ph = 0;
       uint32_t step = 0;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      for (int t = work0; t < total && ok; t += work_step) {
         TileInfo ti;
-        decode_tile<GROUPED, SWAP, BN>(prm, &tm_p, &tm_q, t, ti);
+        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, t, ti);
+        // A pair splits the instruction's N in halves between the two CTAs' shared memory,
+        // so it always issues N = BN (each CTA staged BN/2 rows; rows past the edge are zero).
         int n_mma = ti.q_rows - ti.q0;
-        if (n_mma > BN) n_mma = BN;
+        if (n_mma > BN || CTA2) n_mma = BN;
         n_mma = (n_mma + 15) & ~15;
-        const uint32_t idesc = make_idesc_mxf4nvf4(kBM, n_mma);
+        const uint32_t idesc = make_idesc_mxf4nvf4(CTA2 ? 2 * kBM : kBM, n_mma);
         const uint32_t d_tmem = tmem_base + acc * BN;
         const uint32_t sfq_shift = (ti.q0 & 127) >> 5;
         if (!(prm.debug & 8192) &&
-            !mbar_wait_bounded(acce_bar(acc), aph ^ 1, abort_flag, prm.status, kStatusTimeoutMma,
-                               tmo)) { ok = false; break; }
+            !(CTA2 ? mbar_wait_bounded_cluster(acce_bar(acc), aph ^ 1, abort_flag, prm.status,
+                                               kStatusTimeoutMma, tmo)
+                   : mbar_wait_bounded(acce_bar(acc), aph ^ 1, abort_flag, prm.status,
+                                       kStatusTimeoutMma, tmo))) { ok = false; break; }
         tc_fence_after();
         for (int kt = 0; kt < ti.num_kt; ++kt, ++step) {
           // One wait per stage pair: the scale warps arrive on sf_full only after both
           // stages' data landed and both scale buffers are written.  (Any mbarrier wait
           // in this thread costs ~130 cycles after a tcgen05.commit, so halve them.)
-          if (!(s & 1)) {
-            if (!mbar_wait_bounded(sff_bar(s), ph, abort_flag, prm.status, kStatusTimeoutMma, tmo)) {
+          if (!(step & 1)) {
+            const uint32_t pair = step >> 1;
+            const uint32_t pph = (pair / P) & 1;
+            if (!(CTA2 ? mbar_wait_bounded_cluster(sff_bar(pair), pph, abort_flag, prm.status,
+                                                   kStatusTimeoutMma, tmo)
+                       : mbar_wait_bounded(sff_bar(pair), pph, abort_flag, prm.status,
+                                           kStatusTimeoutMma, tmo))) {
               ok = false;
               break;
             }
@@ -382,33 +424,43 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           }
           trace_event(prm, 1, step);
           const uint32_t sfp_col = tmem_base + C_::kSfCol0 + s * C_::kSfCols;
-          const uint32_t sfq_col = sfp_col + 16 + sfq_shift;
-          const uint64_t pdesc = make_smem_desc(base + stage_off(s), 0, 1024, 2);
-          const uint64_t qdesc = make_smem_desc(base + stage_off(s) + kOffQ, 0, 1024, 2);
+          const uint32_t sfq_col = sfp_col + C_::kSfpCols + sfq_shift;
+          const uint64_t pdesc = make_smem_desc(base + stage_off(s), 0, C_::kSbo, C_::kSwizzle);
+          const uint64_t qdesc = make_smem_desc(base + stage_off(s) + kOffQ, 0, C_::kSbo, C_::kSwizzle);
           const uint32_t acc0 = kt > 0 ? 1u : 0u;
           if (prm.debug & 4) {
-          } else if (k_blocks(ti, kt) == 4) {
+          } else if (k_blocks(ti, kt) == KB) {
 #pragma unroll
-            for (int kb = 0; kb < 4; ++kb)
-              tc_mma_mxf4nvf4(d_tmem, pdesc + 2 * kb, qdesc + 2 * kb, idesc, sfp_col + kb * 4,
-                              sfq_col + kb * C_::kSfqColsPerKb, kb > 0 ? 1u : acc0);
+            for (int kb = 0; kb < KB; ++kb) {
+              if constexpr (CTA2)
+                tc_mma_mxf4nvf4_2cta(d_tmem, pdesc + 2 * kb, qdesc + 2 * kb, idesc, sfp_col + kb * 4,
+                                     sfq_col + kb * C_::kSfqColsPerKb, kb > 0 ? 1u : acc0);
+              else
+                tc_mma_mxf4nvf4(d_tmem, pdesc + 2 * kb, qdesc + 2 * kb, idesc, sfp_col + kb * 4,
+                                sfq_col + kb * C_::kSfqColsPerKb, kb > 0 ? 1u : acc0);
+            }
           } else {
             const int kbv = k_blocks(ti, kt);
-            for (int kb = 0; kb < kbv; ++kb)
-              tc_mma_mxf4nvf4(d_tmem, pdesc + 2 * kb, qdesc + 2 * kb, idesc, sfp_col + kb * 4,
-                              sfq_col + kb * C_::kSfqColsPerKb, kb > 0 ? 1u : acc0);
+            for (int kb = 0; kb < kbv; ++kb) {
+              if constexpr (CTA2)
+                tc_mma_mxf4nvf4_2cta(d_tmem, pdesc + 2 * kb, qdesc + 2 * kb, idesc, sfp_col + kb * 4,
+                                     sfq_col + kb * C_::kSfqColsPerKb, kb > 0 ? 1u : acc0);
+              else
+                tc_mma_mxf4nvf4(d_tmem, pdesc + 2 * kb, qdesc + 2 * kb, idesc, sfp_col + kb * 4,
+                                sfq_col + kb * C_::kSfqColsPerKb, kb > 0 ? 1u : acc0);
+            }
           }
           // release the stage (and its scale buffer) once these MMAs have read it
-          tc_commit(empty_bar(s));
+          if (CTA2) tc_commit_2cta(empty_bar(s)); else tc_commit(empty_bar(s));
           trace_event(prm, 2, step);
           if (++s == S) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
-        tc_commit(accf_bar(acc));
+        if (CTA2) tc_commit_2cta(accf_bar(acc)); else tc_commit(accf_bar(acc));
         if (++acc == A) { acc = 0; aph ^= 1; }
       }
       // wait until every tcgen05 op this thread issued has finished before TMEM is released
-      tc_commit(drain_bar);
+      if (CTA2) tc_commit_2cta(drain_bar); else tc_commit(drain_bar);
       mbar_wait_bounded(drain_bar, 0, abort_flag, prm.status, kStatusTimeoutDrain, tmo);
     }
   } else if (warp >= kFirstSfWarp) {
@@ -427,76 +479,71 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       const int kbv = k_blocks(ti, kt);
       const uint32_t col = tmem_base + lane_base + C_::kSfCol0 + cs * C_::kSfCols;
       const uint8_t* sp = smem + stage_off(cs) + kOffSfp + lane * 16;
-      uint32_t r[16];
+      uint32_t r[4 * KB];
 #pragma unroll
-      for (int kb = 0; kb < 4; ++kb) {
+      for (int kb = 0; kb < KB; ++kb) {
         uint4 v = make_uint4(0, 0, 0, 0);
         if (kb < kbv) v = *reinterpret_cast<const uint4*>(sp + kb * kAtomBytes);
         r[4 * kb + 0] = v.x; r[4 * kb + 1] = v.y; r[4 * kb + 2] = v.z; r[4 * kb + 3] = v.w;
       }
-      tmem_st_32x32b_x16(col, r);
+      tmem_st_32x32b(col, r);
       const uint8_t* sq = smem + stage_off(cs) + kOffSfq + lane * 16;
-      if constexpr (C_::kSfqAtoms == 1) {
+      uint32_t q[KB * C_::kSfqColsPerKb];
 #pragma unroll
-        for (int kb = 0; kb < 4; ++kb) {
+      for (int kb = 0; kb < KB; ++kb)
+#pragma unroll
+        for (int a = 0; a < C_::kSfqAtoms; ++a) {
           uint4 v = make_uint4(0, 0, 0, 0);
-          if (kb < kbv) v = *reinterpret_cast<const uint4*>(sq + kb * kAtomBytes);
-          r[4 * kb + 0] = v.x; r[4 * kb + 1] = v.y; r[4 * kb + 2] = v.z; r[4 * kb + 3] = v.w;
+          if (kb < kbv && a < nq_atoms)
+            v = *reinterpret_cast<const uint4*>(sq + a * KB * kAtomBytes + kb * kAtomBytes);
+          const int o = kb * C_::kSfqColsPerKb + a * 4;
+          q[o + 0] = v.x; q[o + 1] = v.y; q[o + 2] = v.z; q[o + 3] = v.w;
         }
-        tmem_st_32x32b_x16(col + 16, r);
-      } else {
-        uint32_t q[32];
-#pragma unroll
-        for (int kb = 0; kb < 4; ++kb)
-#pragma unroll
-          for (int a = 0; a < 2; ++a) {
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (kb < kbv && a < nq_atoms)
-              v = *reinterpret_cast<const uint4*>(sq + a * 4 * kAtomBytes + kb * kAtomBytes);
-            const int o = kb * 8 + a * 4;
-            q[o + 0] = v.x; q[o + 1] = v.y; q[o + 2] = v.z; q[o + 3] = v.w;
-          }
-        tmem_st_32x32b_x32(col + 16, q);
-      }
+      tmem_st_32x32b(col + C_::kSfpCols, q);
     };
     // The pair a k-stage belongs to is tracked across tiles: a pair can straddle
     // two tiles when a tile has an odd number of k-stages.
     TileInfo pend_ti;
-    int pend_kt = -1, pend_nq = 0;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+    int pend_kt = -1, pend_nq = 0, pend_cs = 0;
+    uint32_t pend_cph = 0;
+    for (int t = work0; t < total && ok; t += work_step) {
       TileInfo ti;
-      decode_tile<GROUPED, SWAP, BN>(prm, &tm_p, &tm_q, t, ti);
+      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, t, ti);
       const int nq_atoms = q_atoms(ti);
       for (int kt = 0; kt < ti.num_kt && ok; ++kt, ++tstep) {
         const int cs = s;
         const uint32_t cph = ph;
         if (++s == S) { s = 0; ph ^= 1; }
-        if (((cs >> 1) & 1) != grp) continue;
-        const bool last = (kt == ti.num_kt - 1) && (t + (int)gridDim.x >= total);
-        if (!(cs & 1) && !last) {  // first stage of the pair: remember it, handle with the second
+        const uint32_t pair = tstep >> 1;  // k-steps 2j and 2j+1 form pair j
+        if ((int)(pair & 1) != grp) continue;
+        const bool last = (kt == ti.num_kt - 1) && (t + work_step >= total);
+        if (!(tstep & 1) && !last) {  // first step of the pair: remember it, handle with the second
           pend_ti = ti;
           pend_kt = kt;
           pend_nq = nq_atoms;
+          pend_cs = cs;
+          pend_cph = cph;
           continue;
         }
         int w_ok = 1;
         if (lane == 0) {
-          if (cs & 1)
-            w_ok = mbar_wait_bounded(full_bar(cs - 1), cph, abort_flag, prm.status, kStatusTimeoutMma, tmo);
+          if (tstep & 1)
+            w_ok = mbar_wait_bounded(full_bar(pend_cs), pend_cph, abort_flag, prm.status,
+                                     kStatusTimeoutMma, tmo);
           w_ok = w_ok && mbar_wait_bounded(full_bar(cs), cph, abort_flag, prm.status, kStatusTimeoutMma, tmo);
         }
         w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
         if (!w_ok) { ok = false; break; }
         tc_fence_after();
         if (!(prm.debug & 8)) {
-          if (cs & 1) write_stage(pend_ti, pend_kt, cs - 1, pend_nq);
+          if (tstep & 1) write_stage(pend_ti, pend_kt, pend_cs, pend_nq);
           write_stage(ti, kt, cs, nq_atoms);
           tmem_st_wait();
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(sff_bar(cs));
+          arrive_leader(sff_bar(pair));
           if ((warp & 3) == 0) trace_event(prm, 3 + grp, tstep);
         }
       }
@@ -516,9 +563,9 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     const int quad = warp & 3;
     const int half = warp >> 2;
     const int row = quad * 32 + lane;  // TMEM lane == accumulator row
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    for (int t = work0; t < total; t += work_step) {
       TileInfo ti;
-      decode_tile<GROUPED, SWAP, BN>(prm, &tm_p, &tm_q, t, ti);
+      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, t, ti);
       if (!mbar_wait_bounded(accf_bar(acc), aph, abort_flag, prm.status, kStatusTimeoutEpilogue,
                              tmo)) break;
       tc_fence_after();
@@ -542,7 +589,8 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         }
       }
       tc_fence_before();
-      mbar_arrive(acce_bar(acc));
+      __syncwarp();
+      if (lane == 0) arrive_leader(acce_bar(acc));
       if (threadIdx.x == 0) trace_event(prm, 5, etile++);
       if (++acc == A) { acc = 0; aph ^= 1; }
       const int p = ti.p0 + row;
@@ -583,10 +631,14 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
 
   tc_fence_before();
   __syncthreads();
+  // Pair: neither CTA leaves (or frees TMEM) while the leader's MMAs may still read the
+  // peer's shared memory or the peer still arrives on the leader's barriers.
+  if (CTA2) cluster_sync();
   if (warp == kMmaWarp) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, C_::kTmemCols);
+    if (CTA2) tmem_dealloc_2cta(tmem_base, C_::kTmemCols);
+    else tmem_dealloc(tmem_base, C_::kTmemCols);
   }
 }
 

@@ -57,11 +57,19 @@ SHAPES = [(72, 136, 64, 1), (200, 100, 192, 2), (129, 257, 320, 1), (64, 512, 10
 CONFIGS = [(1, 64), (1, 128), (1, 256), (2, 64), (2, 128), (2, 256)]
 
 
-@pytest.mark.parametrize("order,bn", CONFIGS)
+CONFIGS += [(2, 64, 128), (2, 128, 128), (1, 128, 128), (1, 256, 128)]  # 128-wide K stages
+CONFIGS += [(2, 64, 0, 2), (2, 128, 0, 2), (1, 128, 0, 2), (1, 256, 0, 2)]  # CTA-pair (M=256) tiles
+
+
+@pytest.mark.parametrize("cfg", CONFIGS)
 @pytest.mark.parametrize("m,n,k,l", SHAPES)
-def test_tile_configs_ragged(cuda, order, bn, m, n, k, l):
+def test_tile_configs_ragged(cuda, cfg, m, n, k, l):
+    order, bn = cfg[0], cfg[1]
+    stage_k = cfg[2] if len(cfg) > 2 else 0
+    pair = cfg[3] if len(cfg) > 3 else 0
     data = inputs.generate_input(m, n, k, l, seed=7)
-    got = _run_dense(data, opt=_native.options(operand_order=order, tile_n=bn))
+    got = _run_dense(data, opt=_native.options(operand_order=order, tile_n=bn, stage_k=stage_k,
+                                               cta_pair=pair))
     assert_close(got, dense_expected(data), f"order={order} bn={bn} {m}x{n}x{k}x{l}")
 
 
@@ -130,12 +138,12 @@ REF_GROUP_CASES = [
 ]
 
 
-@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("bn,stage_k", [(64, 0), (128, 0), (256, 0), (128, 128)])
 @pytest.mark.parametrize("case", range(len(REF_GROUP_CASES)))
-def test_reference_group_cases(cuda, case, bn):
+def test_reference_group_cases(cuda, case, bn, stage_k):
     m, n, k = REF_GROUP_CASES[case]
     gdata = inputs.generate_group_input(m, n, k, len(m), seed=1111)
-    got = _run_grouped(gdata, opt=_native.options(tile_n=bn))
+    got = _run_grouped(gdata, opt=_native.options(tile_n=bn, stage_k=stage_k))
     for g, (x, e) in enumerate(zip(got, _grouped_expected(gdata))):
         assert_close(x, e, f"case {case} group {g}")
 

@@ -57,7 +57,8 @@ typedef struct nvfp4_options {
   int debug;                      /* test/probe bits, 0 in normal use: 1 = issue no loads so every
                                      pipeline wait runs out (status test); 2/4/8/16 = skip data
                                      movement / MMAs / scale stores / output stores (timing probes) */
-  void* trace;                    /* NULL, or device buffer of 12 x 256 uint64 stamps (CTA 0) */
+  void* trace;                    /* NULL, or device buffer of 2 x 8 x 32 uint64 stamps (CTAs 0, 1; low 32 bits of the ns timer),
+                                     followed by 4 stamps per CTA (entry, start, first tile, exit) */
   int stage_k;                    /* 0 = auto; 128 or 256 K elements per pipeline stage */
   int cta_pair;                   /* 0 = auto, 1 = off, 2 = M=256 tiles on a CTA pair (cta_group::2) */
 } nvfp4_options;

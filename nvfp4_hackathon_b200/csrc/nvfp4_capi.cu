@@ -186,13 +186,18 @@ int launch(const CUtensorMap& tp, const CUtensorMap& tq, const GemmParams& prm, 
   static bool attr_done[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
+  // tracing (a debug option) stages its stamps in extra shared memory
+  const int smem = C_::kSmemBytes + (prm.trace ? kTraceSmemBytes : 0);
+  if (smem > kMaxDynamicSmem) return fail(NVFP4_ERR_UNSUPPORTED, "trace does not fit this tile config");
   if (!attr_done[dev]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C_::kSmemBytes + kTraceSmemBytes <= kMaxDynamicSmem
+                                             ? C_::kSmemBytes + kTraceSmemBytes
+                                             : C_::kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     attr_done[dev] = true;
   }
-  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kNumThreads), C_::kSmemBytes, stream,
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kNumThreads), smem, stream,
                              CTA2 ? 2 : 1, tp, tq, prm);
   if (e != cudaSuccess) return cuda_fail(e, "nvfp4_gemm_kernel launch");
   return NVFP4_OK;

@@ -52,7 +52,8 @@ constexpr int kMmaWarp = 10;
 constexpr int kFirstSfWarp = 11;
 constexpr int kSfGroups = 2;        // groups of 4 scale warps; group g serves k-step pairs j % 2 == g
 constexpr int kNumThreads = 32 * (kFirstSfWarp + 4 * kSfGroups);
-constexpr int kSmemBudget = 232448 - 2048;  // dynamic smem per CTA minus alignment/barriers
+constexpr int kMaxDynamicSmem = 232448;     // opt-in dynamic shared memory per CTA on sm_100
+constexpr int kSmemBudget = kMaxDynamicSmem - 2560;  // minus alignment, barriers, trace stamps
 
 // KB = 64-wide K blocks per pipeline stage: 4 (256 K, one 128-byte swizzle row per
 // operand row) or 2 (128 K, 64-byte swizzle).  Smaller stages fit twice as many in
@@ -71,18 +72,27 @@ struct Cfg {
   static constexpr int kSfqAtoms = (BN <= 128) ? 1 : 2;  // 128-row scale blocks per Q tile
   static constexpr int kSfpBytes = KB * kAtomBytes;
   static constexpr int kSfqBytes = kSfqAtoms * KB * kAtomBytes;
-  static constexpr int kStageBytes = kPBytes + kQBytes + kSfpBytes + kSfqBytes;
+  static constexpr int kStageBytes = kPBytes + kQBytes;       // operand tiles of one k-step
+  static constexpr int kSfSlotBytes = kSfpBytes + kSfqBytes;  // scale atoms of one k-step
   static constexpr int kSfqColsPerKb = 4 * kSfqAtoms;
   // TMEM columns of one scale buffer: [SFP kb0..kb(KB-1) (4 columns each)][SFQ kb0..]
   static constexpr int kSfpCols = 4 * KB;
   static constexpr int kSfCols = kSfpCols + KB * kSfqColsPerKb;
   static constexpr int kAccStages = (BN <= 128) ? 2 : 1;
-  // one scale buffer per stage; stages come in pairs released by one commit
-  static constexpr int kStagesSmem = kSmemBudget / kStageBytes;
+  // one TMEM scale buffer per stage
+  static constexpr int kStagesSmem = kSmemBudget / (kStageBytes + kSfSlotBytes);
   static constexpr int kStagesTmem = (512 - kAccStages * BN) / kSfCols;
   static constexpr int kStagesRaw = kStagesSmem < kStagesTmem ? kStagesSmem : kStagesTmem;
   static constexpr int kStagesCap = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr int kStages = kStagesCap;
+  // Scale atoms travel in their own ring of shared-memory slots, loaded kSfLead k-steps
+  // ahead of the step's operand tiles, so the scale warps can move them into TMEM while
+  // the operands are still in flight.  Slot of step j is reused by step j + kSfSlots,
+  // loaded when the producer issues step j + kStages: the MMAs of step j have finished.
+  static constexpr int kSfLeadRaw =
+      (kSmemBudget - kStages * (kStageBytes + kSfSlotBytes)) / kSfSlotBytes;
+  static constexpr int kSfLead = kSfLeadRaw < kStages ? kSfLeadRaw : kStages;
+  static constexpr int kSfSlots = kStages + kSfLead;
   // scale hand-off barriers: pair j of consecutive k-steps uses sf_full[j % kPairBars];
   // kPairBars >= (kStages + 1) / 2 + 1 keeps a barrier from being re-armed for pair
   // j + kPairBars before the MMA issuer consumed pair j (those stages must be refilled first)
@@ -91,12 +101,15 @@ struct Cfg {
   static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64
                                  : kColsNeeded <= 128 ? 128 : kColsNeeded <= 256 ? 256 : 512;
   static constexpr int kSfCol0 = kAccStages * BN;
-  // barriers: full[S], sf_full[S/2], empty[S], acc_full[A], acc_empty[A], drain
-  static constexpr int kNumBars = 2 * kStages + kPairBars + 2 * kAccStages + 1;
+  // barriers: full[S], sf_full[P], empty[S], acc_full[A], acc_empty[A], drain, sf_data[slots]
+  static constexpr int kNumBars = 2 * kStages + kPairBars + 2 * kAccStages + 1 + kSfSlots;
   static constexpr int kBarrierBytes = 8 * kNumBars + 16;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+  static constexpr int kSmemBytes =
+      1024 + kStages * kStageBytes + kSfSlots * kSfSlotBytes + kBarrierBytes;
   static_assert(kStages >= 2, "need at least two stages");
   static_assert(kColsNeeded <= 512, "TMEM budget exceeded");
+  static_assert(kSfSlots <= 32, "slot bookkeeping uses 32-bit masks");
+  static_assert(kSmemBytes + 1024 <= kMaxDynamicSmem, "shared memory budget exceeded (incl. trace)");
 };
 
 // Everything the kernel needs; tensor maps for the dense case are separate
@@ -132,15 +145,25 @@ struct GemmParams {
   unsigned long long* trace;
 };
 
-// trace slots: role r (0 producer, 1 mma-wait-done, 2 mma-issued, 3 sf-group0 done,
-// 4 sf-group1 done, 5 epilogue tile done) x step (< kTraceSteps)
-// (slots 6 x 256 hold the matching clock64 values)
-constexpr int kTraceSteps = 256;
-__device__ __forceinline__ void trace_event(const GemmParams& prm, int role, uint32_t step) {
-  if (prm.trace && blockIdx.x == 0 && step < (uint32_t)kTraceSteps) {
-    prm.trace[role * kTraceSteps + step] = global_timer_ns();
-    prm.trace[(6 + role) * kTraceSteps + step] = clock64();
-  }
+// Trace (debug only).  When GemmParams::trace is set the kernel is launched with
+// kTraceSmemBytes of extra shared memory: every role stamps the low 32 bits of
+// %globaltimer (ns) into
+// shared memory (a global store would delay the next cluster-scope release of the
+// same thread), and at exit CTAs 0 and 1 copy their stamps to
+// trace[(cta * kTraceRoles + role) * kTraceSteps + step].  Roles:
+//   0 producer issued k-step    1 MMA wait done    2 MMA issued    3 / 4 scale group 0 / 1 done
+//   5 epilogue drained tile     6 scale warp: scales written and the pair's operands landed
+// After those, 4 global stamps per CTA (0 entry, 1 after the wait on the previous grid,
+// 2 first accumulator drained, 3 exit).
+constexpr int kTraceSteps = 32;
+constexpr int kTraceRoles = 8;
+constexpr int kTraceSmemBytes = kTraceRoles * kTraceSteps * 4;
+constexpr int kTraceCtaBase = 2 * kTraceRoles * kTraceSteps;
+__device__ __forceinline__ void trace_cta(const GemmParams& prm, int what) {
+  if (prm.trace) prm.trace[kTraceCtaBase + 4 * blockIdx.x + what] = global_timer_ns();
+}
+__device__ __forceinline__ void trace_event(uint32_t* tsm, int role, uint32_t step) {
+  if (tsm && step < (uint32_t)kTraceSteps) tsm[role * kTraceSteps + step] = (uint32_t)global_timer_ns();
 }
 
 // Per-tile view shared by all roles.
@@ -231,12 +254,15 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_addr);
 
-  // stage s: [P | Q | SFP atoms | SFQ atoms]
+  // [stage 0 .. S-1: P | Q] [scale slot 0 .. NS-1: SFP atoms | SFQ atoms] [barriers]
+  constexpr int NS = C_::kSfSlots;
+  constexpr int LEAD = C_::kSfLead;
   auto stage_off = [&](int s) { return (uint32_t)(s * C_::kStageBytes); };
   constexpr uint32_t kOffQ = C_::kPBytes;
-  constexpr uint32_t kOffSfp = C_::kPBytes + C_::kQBytes;
-  constexpr uint32_t kOffSfq = kOffSfp + C_::kSfpBytes;
-  const uint32_t bar_base = base + S * C_::kStageBytes;
+  constexpr uint32_t kSlot0 = S * C_::kStageBytes;
+  auto slot_off = [&](int j) { return kSlot0 + (uint32_t)(j * C_::kSfSlotBytes); };
+  constexpr uint32_t kOffSfq = C_::kSfpBytes;  // within a slot
+  const uint32_t bar_base = base + kSlot0 + NS * C_::kSfSlotBytes;
   auto full_bar = [&](int s) { return bar_base + 8 * s; };
   constexpr int P = C_::kPairBars;
   auto sff_bar = [&](uint32_t pair) { return bar_base + 8 * (S + pair % P); };  // per k-step pair
@@ -244,12 +270,17 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   auto accf_bar = [&](int a) { return bar_base + 8 * (2 * S + P + a); };
   auto acce_bar = [&](int a) { return bar_base + 8 * (2 * S + P + A + a); };
   const uint32_t drain_bar = bar_base + 8 * (2 * S + P + 2 * A);
-  uint8_t* bar_ptr = smem + S * C_::kStageBytes;
+  auto sfd_bar = [&](int j) { return bar_base + 8 * (2 * S + P + 2 * A + 1 + j); };
+  uint8_t* bar_ptr = smem + kSlot0 + NS * C_::kSfSlotBytes;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bar_ptr + 8 * C_::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + 8 * C_::kNumBars + 4);
+  uint32_t* tsm = prm.trace ? reinterpret_cast<uint32_t*>(bar_ptr + C_::kBarrierBytes) : nullptr;
+  if (tsm)
+    for (int i = threadIdx.x; i < kTraceRoles * kTraceSteps; i += blockDim.x) tsm[i] = 0u;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) trace_cta(prm, 0);
   pdl_launch_dependents();
   // CTA pairs: rank 0 (leader) issues the MMAs for both; tiles are walked per pair.
   const uint32_t crank = CTA2 ? cluster_ctarank() : 0;
@@ -274,6 +305,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       mbar_init(acce_bar(a), kEpiWarps * (CTA2 ? 2 : 1));
     }
     mbar_init(drain_bar, 1);
+    for (int j = 0; j < NS; ++j) mbar_init(sfd_bar(j), 1);
     *abort_flag = 0;
     fence_mbar_init();
     fence_async_shared();
@@ -300,6 +332,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   // overlaps the previous kernel on the stream; global memory is used only after
   // that kernel has completed.
   pdl_wait_prior_grid();
+  if (threadIdx.x == 0) trace_cta(prm, 1);
 
   const int total = GROUPED ? __ldg(prm.tile_prefix + prm.G) : prm.total_tiles;
   const uint64_t tmo = prm.timeout_ns;
@@ -329,7 +362,53 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       const void* last_map = nullptr;
       bool ok = true;
       uint32_t issued_mask = 0, issued_par = 0;
-      uint32_t pstep = 0;
+      // Cursor over this CTA's k-steps (tile, k-stage) LEAD steps ahead of the operand
+      // loads: the scale atoms of that step go into its slot of the scale ring.
+      struct Cursor {
+        int t, kt;
+        TileInfo ti;
+      };
+      auto cur_next = [&](Cursor& c) {
+        if (++c.kt == c.ti.num_kt) {
+          c.kt = 0;
+          c.t += work_step;
+          if (c.t < total) decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, c.t, c.ti);
+        }
+      };
+      Cursor sfc;
+      sfc.t = work0;
+      sfc.kt = 0;
+      if (sfc.t < total) decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sfc.t, sfc.ti);
+      int sl = 0;
+      uint32_t slph = 0;
+      uint32_t sf_issued = 0, sf_par = 0;
+      auto issue_sf = [&](const Cursor& c) {
+        const uint32_t bar = sfd_bar(sl);
+        if (prm.debug & 2) {  // timing probe: no data movement
+          mbar_arrive(bar);
+          return;
+        }
+        const uint32_t sf_bytes = k_blocks(c.ti, c.kt) * kAtomBytes;
+        const int nq = q_atoms(c.ti);
+        const uint32_t dst = base + slot_off(sl);
+        mbar_arrive_expect_tx(bar, sf_bytes * (1 + nq));
+        bulk_load(dst, c.ti.sf_p + ((long long)(c.ti.p0 >> 7) * c.ti.rk + c.kt * KB) * kAtomBytes,
+                  sf_bytes, bar, pol_keep);
+        for (int a = 0; a < nq; ++a)
+          bulk_load(dst + kOffSfq + a * KB * kAtomBytes,
+                    c.ti.sf_q + ((long long)((c.ti.q0 >> 7) + a) * c.ti.rk + c.kt * KB) * kAtomBytes,
+                    sf_bytes, bar, pol_keep);
+        sf_issued |= 1u << sl;
+        sf_par = (sf_par & ~(1u << sl)) | (slph << sl);
+      };
+      auto sf_step = [&](bool mine) {  // the cursor's step: issue if it is ours, then advance
+        if (sfc.t >= total) return;
+        if (mine) issue_sf(sfc);
+        if (++sl == NS) { sl = 0; slph ^= 1; }
+        cur_next(sfc);
+      };
+      // scale atoms of steps 0 .. LEAD-1 go out first (their slots are fresh)
+      for (int j = 0; j < LEAD; ++j) sf_step((j & 1) == (int)pid);
       for (int t = work0; t < total && ok; t += work_step) {
         TileInfo ti;
         decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, t, ti);
@@ -338,38 +417,27 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           tmap_fence_acquire(ti.map_q);
           last_map = ti.map_p;
         }
-        const int pblk = ti.p0 >> 7;
-        const int qblk = ti.q0 >> 7;
-        const int nq_atoms = q_atoms(ti);
         for (int kt = 0; kt < ti.num_kt; ++kt, ++gstep) {
-          if ((gstep & 1) != pid) {  // the other producer's step (S is even: stage parity == step parity)
-            if (++s == S) { s = 0; ph ^= 1; }
-            continue;
+          const bool mine = (gstep & 1) == pid;
+          if (mine) {
+            // stage s free: the MMAs of step gstep - S are done (and with them every read
+            // of the scale slot step gstep + LEAD reuses)
+            if (!mbar_wait_bounded(empty_bar(s), ph ^ 1, abort_flag, prm.status,
+                                   kStatusTimeoutProducer, tmo)) { ok = false; break; }
+            if (prm.debug & 2) {  // timing probe: no data movement
+              mbar_arrive(full_bar(s));
+            } else {
+              const uint32_t st = base + stage_off(s);
+              mbar_arrive_expect_tx(full_bar(s), C_::kPBytes + C_::kQBytes);
+              tma_load_3d(st, ti.map_p, full_bar(s), kt * C_::kBKBytes, ti.p0, ti.l, pol_keep);
+              tma_load_3d(st + kOffQ, ti.map_q, full_bar(s), kt * C_::kBKBytes,
+                          ti.q0 + (int)crank * C_::kQRows, ti.l, pol_keep);
+              issued_mask |= 1u << s;
+              issued_par = (issued_par & ~(1u << s)) | (ph << s);
+            }
+            trace_event(tsm, 0, gstep);
           }
-          if (!mbar_wait_bounded(empty_bar(s), ph ^ 1, abort_flag, prm.status,
-                                 kStatusTimeoutProducer, tmo)) { ok = false; break; }
-          if (prm.debug & 2) {  // timing probe: no data movement
-            mbar_arrive(full_bar(s));
-            if (++s == S) { s = 0; ph ^= 1; }
-            continue;
-          }
-          const uint32_t sf_bytes = k_blocks(ti, kt) * kAtomBytes;
-          const uint32_t bytes = C_::kPBytes + C_::kQBytes + sf_bytes * (1 + nq_atoms);
-          const uint32_t st = base + stage_off(s);
-          mbar_arrive_expect_tx(full_bar(s), bytes);
-          tma_load_3d(st, ti.map_p, full_bar(s), kt * C_::kBKBytes, ti.p0, ti.l, pol_keep);
-          tma_load_3d(st + kOffQ, ti.map_q, full_bar(s), kt * C_::kBKBytes,
-                      ti.q0 + (int)crank * C_::kQRows, ti.l, pol_keep);
-          bulk_load(st + kOffSfp, ti.sf_p + ((long long)pblk * ti.rk + kt * KB) * kAtomBytes,
-                    sf_bytes, full_bar(s), pol_keep);
-          for (int a = 0; a < nq_atoms; ++a)
-            bulk_load(st + kOffSfq + a * KB * kAtomBytes,
-                      ti.sf_q + ((long long)(qblk + a) * ti.rk + kt * KB) * kAtomBytes, sf_bytes,
-                      full_bar(s), pol_keep);
-          if (pid == 0) trace_event(prm, 0, pstep);
-          pstep += 1;
-          issued_mask |= 1u << s;
-          issued_par = (issued_par & ~(1u << s)) | (ph << s);
+          sf_step(mine);
           if (++s == S) { s = 0; ph ^= 1; }
         }
       }
@@ -378,6 +446,9 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         for (int i = 0; i < S; ++i)
           if (issued_mask & (1u << i))
             mbar_wait_plain(full_bar(i), (issued_par >> i) & 1u, 100000000ull);
+        for (int i = 0; i < NS; ++i)
+          if (sf_issued & (1u << i))
+            mbar_wait_plain(sfd_bar(i), (sf_par >> i) & 1u, 100000000ull);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -422,7 +493,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
             }
             tc_fence_after();
           }
-          trace_event(prm, 1, step);
+          trace_event(tsm, 1, step);
           const uint32_t sfp_col = tmem_base + C_::kSfCol0 + s * C_::kSfCols;
           const uint32_t sfq_col = sfp_col + C_::kSfpCols + sfq_shift;
           const uint64_t pdesc = make_smem_desc(base + stage_off(s), 0, C_::kSbo, C_::kSwizzle);
@@ -452,7 +523,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           }
           // release the stage (and its scale buffer) once these MMAs have read it
           if (CTA2) tc_commit_2cta(empty_bar(s)); else tc_commit(empty_bar(s));
-          trace_event(prm, 2, step);
+          trace_event(tsm, 2, step);
           if (++s == S) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
@@ -475,20 +546,22 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     int s = 0;
     uint32_t ph = 0;
     bool ok = true;
-    auto write_stage = [&](const TileInfo& ti, int kt, int cs, int nq_atoms) {
+    // Scale factors of one k-stage in registers: lane l holds row l of every atom
+    // (16 bytes = 4 TMEM columns per atom), read from the stage in shared memory.
+    struct SfRegs {
+      uint32_t p[4 * KB];
+      uint32_t q[KB * C_::kSfqColsPerKb];
+    };
+    auto load_stage = [&](const TileInfo& ti, int kt, int slot, int nq_atoms, SfRegs& r) {
       const int kbv = k_blocks(ti, kt);
-      const uint32_t col = tmem_base + lane_base + C_::kSfCol0 + cs * C_::kSfCols;
-      const uint8_t* sp = smem + stage_off(cs) + kOffSfp + lane * 16;
-      uint32_t r[4 * KB];
+      const uint8_t* sp = smem + slot_off(slot) + lane * 16;
+      const uint8_t* sq = sp + kOffSfq;
 #pragma unroll
       for (int kb = 0; kb < KB; ++kb) {
         uint4 v = make_uint4(0, 0, 0, 0);
         if (kb < kbv) v = *reinterpret_cast<const uint4*>(sp + kb * kAtomBytes);
-        r[4 * kb + 0] = v.x; r[4 * kb + 1] = v.y; r[4 * kb + 2] = v.z; r[4 * kb + 3] = v.w;
+        r.p[4 * kb + 0] = v.x; r.p[4 * kb + 1] = v.y; r.p[4 * kb + 2] = v.z; r.p[4 * kb + 3] = v.w;
       }
-      tmem_st_32x32b(col, r);
-      const uint8_t* sq = smem + stage_off(cs) + kOffSfq + lane * 16;
-      uint32_t q[KB * C_::kSfqColsPerKb];
 #pragma unroll
       for (int kb = 0; kb < KB; ++kb)
 #pragma unroll
@@ -497,14 +570,22 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           if (kb < kbv && a < nq_atoms)
             v = *reinterpret_cast<const uint4*>(sq + a * KB * kAtomBytes + kb * kAtomBytes);
           const int o = kb * C_::kSfqColsPerKb + a * 4;
-          q[o + 0] = v.x; q[o + 1] = v.y; q[o + 2] = v.z; q[o + 3] = v.w;
+          r.q[o + 0] = v.x; r.q[o + 1] = v.y; r.q[o + 2] = v.z; r.q[o + 3] = v.w;
         }
-      tmem_st_32x32b(col + C_::kSfpCols, q);
     };
-    // The pair a k-stage belongs to is tracked across tiles: a pair can straddle
-    // two tiles when a tile has an odd number of k-stages.
-    TileInfo pend_ti;
-    int pend_kt = -1, pend_nq = 0, pend_cs = 0;
+    auto store_stage = [&](int cs, SfRegs& r) {
+      const uint32_t col = tmem_base + lane_base + C_::kSfCol0 + cs * C_::kSfCols;
+      tmem_st_32x32b(col, r.p);
+      tmem_st_32x32b(col + C_::kSfpCols, r.q);
+    };
+    // Per k-step: wait until the step's TMEM scale buffer is free (the MMAs of step
+    // tstep - S are done) and its scale atoms landed in their slot, then write them.
+    // Per pair of k-steps (tracked across tiles: a pair straddles two tiles when a tile
+    // has an odd number of k-stages): after both steps' scales are written, wait for both
+    // steps' operand tiles and arrive once on the pair's sf_full.
+    int sl = 0;
+    uint32_t slph = 0;
+    int pend_cs = 0;
     uint32_t pend_cph = 0;
     for (int t = work0; t < total && ok; t += work_step) {
       TileInfo ti;
@@ -514,18 +595,33 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         const int cs = s;
         const uint32_t cph = ph;
         if (++s == S) { s = 0; ph ^= 1; }
+        const int cslot = sl;
+        const uint32_t cslph = slph;
+        if (++sl == NS) { sl = 0; slph ^= 1; }
         const uint32_t pair = tstep >> 1;  // k-steps 2j and 2j+1 form pair j
         if ((int)(pair & 1) != grp) continue;
         const bool last = (kt == ti.num_kt - 1) && (t + work_step >= total);
-        if (!(tstep & 1) && !last) {  // first step of the pair: remember it, handle with the second
-          pend_ti = ti;
-          pend_kt = kt;
-          pend_nq = nq_atoms;
+        const bool first = !(tstep & 1) && !last;  // the pair's second step follows
+        int w_ok = 1;
+        if (lane == 0)
+          w_ok = mbar_wait_bounded(empty_bar(cs), cph ^ 1, abort_flag, prm.status,
+                                   kStatusTimeoutMma, tmo) &&
+                 mbar_wait_bounded(sfd_bar(cslot), cslph, abort_flag, prm.status,
+                                   kStatusTimeoutMma, tmo);
+        w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+        if (!w_ok) { ok = false; break; }
+        tc_fence_after();
+        if (!(prm.debug & 8)) {
+          SfRegs r;
+          load_stage(ti, kt, cslot, nq_atoms, r);
+          store_stage(cs, r);
+        }
+        if (first) {
           pend_cs = cs;
           pend_cph = cph;
           continue;
         }
-        int w_ok = 1;
+        if (!(prm.debug & 8)) tmem_st_wait();
         if (lane == 0) {
           if (tstep & 1)
             w_ok = mbar_wait_bounded(full_bar(pend_cs), pend_cph, abort_flag, prm.status,
@@ -534,17 +630,12 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         }
         w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
         if (!w_ok) { ok = false; break; }
-        tc_fence_after();
-        if (!(prm.debug & 8)) {
-          if (tstep & 1) write_stage(pend_ti, pend_kt, pend_cs, pend_nq);
-          write_stage(ti, kt, cs, nq_atoms);
-          tmem_st_wait();
-        }
+        if (lane == 0 && (warp & 3) == 0) trace_event(tsm, 6, tstep);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           arrive_leader(sff_bar(pair));
-          if ((warp & 3) == 0) trace_event(prm, 3 + grp, tstep);
+          if ((warp & 3) == 0) trace_event(tsm, 3 + grp, tstep);
         }
       }
     }
@@ -591,7 +682,10 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       tc_fence_before();
       __syncwarp();
       if (lane == 0) arrive_leader(acce_bar(acc));
-      if (threadIdx.x == 0) trace_event(prm, 5, etile++);
+      if (threadIdx.x == 0) {
+        if (etile == 0) trace_cta(prm, 2);
+        trace_event(tsm, 5, etile++);
+      }
       if (++acc == A) { acc = 0; aph ^= 1; }
       const int p = ti.p0 + row;
       if (p < ti.p_rows && !(prm.debug & 16)) {
@@ -631,6 +725,10 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace_cta(prm, 3);
+  if (tsm && blockIdx.x < 2)
+    for (int i = threadIdx.x; i < kTraceRoles * kTraceSteps; i += blockDim.x)
+      prm.trace[blockIdx.x * kTraceRoles * kTraceSteps + i] = tsm[i];
   // Pair: neither CTA leaves (or frees TMEM) while the leader's MMAs may still read the
   // peer's shared memory or the peer still arrives on the leader's barriers.
   if (CTA2) cluster_sync();

@@ -17,15 +17,19 @@
 //               accumulator into registers as fp16, releases the accumulator, then stores
 //               to global while the next tile's MMAs already run
 //   warps 8-9   producers (alternating k-stages): TMA loads of the P and Q tiles (128-byte
-//               swizzle) and plain bulk copies of the scale atoms into a ring of kStages stages
-//   warp 10     TMEM owner and MMA issuer: tcgen05.mma kind::mxf4nvf4 (K = 64 per
-//               instruction), one tcgen05.commit per stage to release it.
-//   warps 11-18 scale warps, two groups of four (group g serves k-step pairs j with j % 2 == g):
-//               each warp moves the stage's scale atoms from shared memory into its own 32
-//               TMEM lanes with ld.shared + tcgen05.st.  (tcgen05.cp costs ~115 cycles per
-//               512-byte atom on the copy engine; register stores run alongside the MMAs.)
-//               Scale buffer s belongs to stage s, so "stage s refilled" already implies
-//               that the MMAs that read the buffer's previous contents have finished.
+//               swizzle) into a ring of kStages stages, and plain bulk copies of the scale
+//               atoms into their own ring of slots, kSfLead k-steps ahead of the operands
+//   warp 10     TMEM owner and MMA issuer: per k-step it waits for the stage's operand
+//               tiles (full) and scales (sf_full), issues tcgen05.mma kind::mxf4nvf4
+//               (K = 64 per instruction) and one tcgen05.commit to release the stage.
+//   warps 11-18 scale warps, two groups of four (group g serves k-steps j with j % 2 == g):
+//               each warp moves the step's scale atoms from their slot into its own 32
+//               TMEM lanes with ld.shared + tcgen05.st, once the step's TMEM scale buffer
+//               is free (the stage's previous MMAs committed).  tcgen05.cp would run in
+//               the MMA's own queue (~56 cycles per 512-byte atom, not overlapped with the
+//               MMAs), register stores run alongside them.
+//   CTA pairs (cta_group::2, M = 256): the leader issues the MMAs; both CTAs' tensor loads
+//   count on the leader's full barrier and both CTAs' scale warps arrive on its sf_full.
 //
 // Scale factors arrive in the reference's pre-permuted layout
 // (kernels/gemm/reference.py:113-150): per 128-row block and per 64-wide K block
@@ -50,7 +54,7 @@ constexpr int kProducerWarp = 8;   // warps 8 and 9: stage issue alternates betw
 constexpr int kNumProducers = 2;
 constexpr int kMmaWarp = 10;
 constexpr int kFirstSfWarp = 11;
-constexpr int kSfGroups = 2;        // groups of 4 scale warps; group g serves k-step pairs j % 2 == g
+constexpr int kSfGroups = 2;        // groups of 4 scale warps; group g serves k-steps j % 2 == g
 constexpr int kNumThreads = 32 * (kFirstSfWarp + 4 * kSfGroups);
 constexpr int kMaxDynamicSmem = 232448;     // opt-in dynamic shared memory per CTA on sm_100
 constexpr int kSmemBudget = kMaxDynamicSmem - 2560;  // minus alignment, barriers, trace stamps
@@ -93,16 +97,12 @@ struct Cfg {
       (kSmemBudget - kStages * (kStageBytes + kSfSlotBytes)) / kSfSlotBytes;
   static constexpr int kSfLead = kSfLeadRaw < kStages ? kSfLeadRaw : kStages;
   static constexpr int kSfSlots = kStages + kSfLead;
-  // scale hand-off barriers: pair j of consecutive k-steps uses sf_full[j % kPairBars];
-  // kPairBars >= (kStages + 1) / 2 + 1 keeps a barrier from being re-armed for pair
-  // j + kPairBars before the MMA issuer consumed pair j (those stages must be refilled first)
-  static constexpr int kPairBars = kStages / 2 + 1;
   static constexpr int kColsNeeded = kAccStages * BN + kStages * kSfCols;
   static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64
                                  : kColsNeeded <= 128 ? 128 : kColsNeeded <= 256 ? 256 : 512;
   static constexpr int kSfCol0 = kAccStages * BN;
-  // barriers: full[S], sf_full[P], empty[S], acc_full[A], acc_empty[A], drain, sf_data[slots]
-  static constexpr int kNumBars = 2 * kStages + kPairBars + 2 * kAccStages + 1 + kSfSlots;
+  // barriers: full[S], sf_full[S], empty[S], acc_full[A], acc_empty[A], drain, sf_data[slots]
+  static constexpr int kNumBars = 3 * kStages + 2 * kAccStages + 1 + kSfSlots;
   static constexpr int kBarrierBytes = 8 * kNumBars + 16;
   static constexpr int kSmemBytes =
       1024 + kStages * kStageBytes + kSfSlots * kSfSlotBytes + kBarrierBytes;
@@ -139,6 +139,7 @@ struct GemmParams {
   // Probe bits (timing experiments and the timeout test; 0 in normal use):
   //   1 producer issues nothing (every wait must time out)   2 no data movement
   //   4 no MMAs   8 no scale stores   16 no epilogue stores
+  // bits 20..30: first k-step of the trace window (trace only)
   int debug;
   // When non-null, CTA 0 records %globaltimer stamps of its pipeline events here
   // (slot layout in trace_slot()); used to measure hand-off latencies.
@@ -152,7 +153,8 @@ struct GemmParams {
 // same thread), and at exit CTAs 0 and 1 copy their stamps to
 // trace[(cta * kTraceRoles + role) * kTraceSteps + step].  Roles:
 //   0 producer issued k-step    1 MMA wait done    2 MMA issued    3 / 4 scale group 0 / 1 done
-//   5 epilogue drained tile     6 scale warp: scales written and the pair's operands landed
+//   5 epilogue drained tile     6 scale warp: scales written
+//   7 last scale warp of the CTA arrived for the step
 // After those, 4 global stamps per CTA (0 entry, 1 after the wait on the previous grid,
 // 2 first accumulator drained, 3 exit).
 constexpr int kTraceSteps = 32;
@@ -164,6 +166,11 @@ __device__ __forceinline__ void trace_cta(const GemmParams& prm, int what) {
 }
 __device__ __forceinline__ void trace_event(uint32_t* tsm, int role, uint32_t step) {
   if (tsm && step < (uint32_t)kTraceSteps) tsm[role * kTraceSteps + step] = (uint32_t)global_timer_ns();
+}
+// latest of several threads' stamps (wrap-around of the 32-bit ns counter ignored)
+__device__ __forceinline__ void trace_event_max(uint32_t* tsm, int role, uint32_t step) {
+  if (tsm && step < (uint32_t)kTraceSteps)
+    atomicMax(tsm + role * kTraceSteps + step, (uint32_t)global_timer_ns());
 }
 
 // Per-tile view shared by all roles.
@@ -264,17 +271,18 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   constexpr uint32_t kOffSfq = C_::kSfpBytes;  // within a slot
   const uint32_t bar_base = base + kSlot0 + NS * C_::kSfSlotBytes;
   auto full_bar = [&](int s) { return bar_base + 8 * s; };
-  constexpr int P = C_::kPairBars;
-  auto sff_bar = [&](uint32_t pair) { return bar_base + 8 * (S + pair % P); };  // per k-step pair
-  auto empty_bar = [&](int s) { return bar_base + 8 * (S + P + s); };
-  auto accf_bar = [&](int a) { return bar_base + 8 * (2 * S + P + a); };
-  auto acce_bar = [&](int a) { return bar_base + 8 * (2 * S + P + A + a); };
-  const uint32_t drain_bar = bar_base + 8 * (2 * S + P + 2 * A);
-  auto sfd_bar = [&](int j) { return bar_base + 8 * (2 * S + P + 2 * A + 1 + j); };
+  auto sff_bar = [&](int s) { return bar_base + 8 * (S + s); };  // scales of stage s in TMEM
+  auto empty_bar = [&](int s) { return bar_base + 8 * (2 * S + s); };
+  auto accf_bar = [&](int a) { return bar_base + 8 * (3 * S + a); };
+  auto acce_bar = [&](int a) { return bar_base + 8 * (3 * S + A + a); };
+  const uint32_t drain_bar = bar_base + 8 * (3 * S + 2 * A);
+  auto sfd_bar = [&](int j) { return bar_base + 8 * (3 * S + 2 * A + 1 + j); };
   uint8_t* bar_ptr = smem + kSlot0 + NS * C_::kSfSlotBytes;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bar_ptr + 8 * C_::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + 8 * C_::kNumBars + 4);
   uint32_t* tsm = prm.trace ? reinterpret_cast<uint32_t*>(bar_ptr + C_::kBarrierBytes) : nullptr;
+  // the trace window starts at k-step (debug >> 20) (tiles for the epilogue role)
+  const uint32_t tbase = (uint32_t)prm.debug >> 20;
   if (tsm)
     for (int i = threadIdx.x; i < kTraceRoles * kTraceSteps; i += blockDim.x) tsm[i] = 0u;
 
@@ -294,12 +302,13 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   };
 
   if (threadIdx.x == 0) {
+    // one arrive per scale warp of the group serving the stage (of both CTAs of a pair),
+    // one per epilogue warp
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
+      mbar_init(sff_bar(s), CTA2 ? 8 : 4);
       mbar_init(empty_bar(s), 1);
     }
-    // one arrive per scale warp (of both CTAs of a pair), one per epilogue warp
-    for (int b = 0; b < P; ++b) mbar_init(sff_bar(b), CTA2 ? 8 : 4);
     for (int a = 0; a < A; ++a) {
       mbar_init(accf_bar(a), 1);
       mbar_init(acce_bar(a), kEpiWarps * (CTA2 ? 2 : 1));
@@ -428,14 +437,25 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
               mbar_arrive(full_bar(s));
             } else {
               const uint32_t st = base + stage_off(s);
-              mbar_arrive_expect_tx(full_bar(s), C_::kPBytes + C_::kQBytes);
-              tma_load_3d(st, ti.map_p, full_bar(s), kt * C_::kBKBytes, ti.p0, ti.l, pol_keep);
-              tma_load_3d(st + kOffQ, ti.map_q, full_bar(s), kt * C_::kBKBytes,
-                          ti.q0 + (int)crank * C_::kQRows, ti.l, pol_keep);
-              issued_mask |= 1u << s;
-              issued_par = (issued_par & ~(1u << s)) | (ph << s);
+              if constexpr (CTA2) {
+                // both CTAs' tiles count on the leader's full barrier, which the MMA waits on
+                if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * (C_::kPBytes + C_::kQBytes));
+                const uint32_t fb = mapa_shared(full_bar(s), 0);
+                tma_load_3d_pair(st, ti.map_p, fb, kt * C_::kBKBytes, ti.p0, ti.l, pol_keep);
+                tma_load_3d_pair(st + kOffQ, ti.map_q, fb, kt * C_::kBKBytes,
+                                 ti.q0 + (int)crank * C_::kQRows, ti.l, pol_keep);
+              } else {
+                mbar_arrive_expect_tx(full_bar(s), C_::kPBytes + C_::kQBytes);
+                tma_load_3d(st, ti.map_p, full_bar(s), kt * C_::kBKBytes, ti.p0, ti.l, pol_keep);
+                tma_load_3d(st + kOffQ, ti.map_q, full_bar(s), kt * C_::kBKBytes,
+                            ti.q0 + (int)crank * C_::kQRows, ti.l, pol_keep);
+              }
+              if (!CTA2 || leader) {  // (a peer cannot wait on the leader's barrier)
+                issued_mask |= 1u << s;
+                issued_par = (issued_par & ~(1u << s)) | (ph << s);
+              }
             }
-            trace_event(tsm, 0, gstep);
+            trace_event(tsm, 0, gstep - tbase);
           }
           sf_step(mine);
           if (++s == S) { s = 0; ph ^= 1; }
@@ -471,29 +491,23 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         const uint32_t idesc = make_idesc_mxf4nvf4(CTA2 ? 2 * kBM : kBM, n_mma);
         const uint32_t d_tmem = tmem_base + acc * BN;
         const uint32_t sfq_shift = (ti.q0 & 127) >> 5;
+        // (CTA-scope acquire also for the pair's barriers, which the peer arrives on: the
+        // data they publish is ordered by the tcgen05 fences and the TMA transaction
+        // counts, and a cluster-scope acquire costs ~0.2 us per wait)
         if (!(prm.debug & 8192) &&
-            !(CTA2 ? mbar_wait_bounded_cluster(acce_bar(acc), aph ^ 1, abort_flag, prm.status,
-                                               kStatusTimeoutMma, tmo)
-                   : mbar_wait_bounded(acce_bar(acc), aph ^ 1, abort_flag, prm.status,
-                                       kStatusTimeoutMma, tmo))) { ok = false; break; }
+            !mbar_wait_bounded(acce_bar(acc), aph ^ 1, abort_flag, prm.status, kStatusTimeoutMma,
+                               tmo)) { ok = false; break; }
         tc_fence_after();
         for (int kt = 0; kt < ti.num_kt; ++kt, ++step) {
-          // One wait per stage pair: the scale warps arrive on sf_full only after both
-          // stages' data landed and both scale buffers are written.  (Any mbarrier wait
-          // in this thread costs ~130 cycles after a tcgen05.commit, so halve them.)
-          if (!(step & 1)) {
-            const uint32_t pair = step >> 1;
-            const uint32_t pph = (pair / P) & 1;
-            if (!(CTA2 ? mbar_wait_bounded_cluster(sff_bar(pair), pph, abort_flag, prm.status,
-                                                   kStatusTimeoutMma, tmo)
-                       : mbar_wait_bounded(sff_bar(pair), pph, abort_flag, prm.status,
-                                           kStatusTimeoutMma, tmo))) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
+          // the operand tiles landed (a pair's full barrier counts both CTAs' bytes) and
+          // the stage's scales are in TMEM
+          if (!mbar_wait_bounded(full_bar(s), ph, abort_flag, prm.status, kStatusTimeoutMma, tmo) ||
+              !mbar_wait_bounded(sff_bar(s), ph, abort_flag, prm.status, kStatusTimeoutMma, tmo)) {
+            ok = false;
+            break;
           }
-          trace_event(tsm, 1, step);
+          tc_fence_after();
+          trace_event(tsm, 1, step - tbase);
           const uint32_t sfp_col = tmem_base + C_::kSfCol0 + s * C_::kSfCols;
           const uint32_t sfq_col = sfp_col + C_::kSfpCols + sfq_shift;
           const uint64_t pdesc = make_smem_desc(base + stage_off(s), 0, C_::kSbo, C_::kSwizzle);
@@ -523,7 +537,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           }
           // release the stage (and its scale buffer) once these MMAs have read it
           if (CTA2) tc_commit_2cta(empty_bar(s)); else tc_commit(empty_bar(s));
-          trace_event(tsm, 2, step);
+          trace_event(tsm, 2, step - tbase);
           if (++s == S) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
@@ -537,9 +551,6 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   } else if (warp >= kFirstSfWarp) {
     if (!(prm.debug & 4096)) {  // (probe bit 4096: scale warps idle)
     // -------------------------------------------------------------- scale warps
-    // Group g serves stage pair g (stages 2g, 2g+1), group 1-g the next pair, and
-    // so on around the ring.  A warp waits for the pair's data, writes both scale
-    // buffers into its TMEM quarter, then arrives once on the pair's sf_full.
     const int grp = (warp - kFirstSfWarp) >> 2;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM quarter
     uint32_t tstep = 0;
@@ -578,15 +589,11 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       tmem_st_32x32b(col, r.p);
       tmem_st_32x32b(col + C_::kSfpCols, r.q);
     };
-    // Per k-step: wait until the step's TMEM scale buffer is free (the MMAs of step
-    // tstep - S are done) and its scale atoms landed in their slot, then write them.
-    // Per pair of k-steps (tracked across tiles: a pair straddles two tiles when a tile
-    // has an odd number of k-stages): after both steps' scales are written, wait for both
-    // steps' operand tiles and arrive once on the pair's sf_full.
+    // Group g serves the k-steps j with j % 2 == g.  Per step: wait until the step's TMEM
+    // scale buffer is free (the MMAs of step j - S are done) and its scale atoms landed in
+    // their slot, write them, and arrive on the stage's sf_full (the leader's, for a pair).
     int sl = 0;
     uint32_t slph = 0;
-    int pend_cs = 0;
-    uint32_t pend_cph = 0;
     for (int t = work0; t < total && ok; t += work_step) {
       TileInfo ti;
       decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, t, ti);
@@ -598,10 +605,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         const int cslot = sl;
         const uint32_t cslph = slph;
         if (++sl == NS) { sl = 0; slph ^= 1; }
-        const uint32_t pair = tstep >> 1;  // k-steps 2j and 2j+1 form pair j
-        if ((int)(pair & 1) != grp) continue;
-        const bool last = (kt == ti.num_kt - 1) && (t + work_step >= total);
-        const bool first = !(tstep & 1) && !last;  // the pair's second step follows
+        if ((int)(tstep & 1) != grp) continue;
         int w_ok = 1;
         if (lane == 0)
           w_ok = mbar_wait_bounded(empty_bar(cs), cph ^ 1, abort_flag, prm.status,
@@ -615,27 +619,15 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           SfRegs r;
           load_stage(ti, kt, cslot, nq_atoms, r);
           store_stage(cs, r);
+          tmem_st_wait();
         }
-        if (first) {
-          pend_cs = cs;
-          pend_cph = cph;
-          continue;
-        }
-        if (!(prm.debug & 8)) tmem_st_wait();
-        if (lane == 0) {
-          if (tstep & 1)
-            w_ok = mbar_wait_bounded(full_bar(pend_cs), pend_cph, abort_flag, prm.status,
-                                     kStatusTimeoutMma, tmo);
-          w_ok = w_ok && mbar_wait_bounded(full_bar(cs), cph, abort_flag, prm.status, kStatusTimeoutMma, tmo);
-        }
-        w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
-        if (!w_ok) { ok = false; break; }
-        if (lane == 0 && (warp & 3) == 0) trace_event(tsm, 6, tstep);
+        if (lane == 0 && (warp & 3) == 0) trace_event(tsm, 6, tstep - tbase);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          arrive_leader(sff_bar(pair));
-          if ((warp & 3) == 0) trace_event(tsm, 3 + grp, tstep);
+          arrive_leader(sff_bar(cs));
+          if ((warp & 3) == 0) trace_event(tsm, 3 + grp, tstep - tbase);
+          trace_event_max(tsm, 7, tstep - tbase);
         }
       }
     }
@@ -684,7 +676,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       if (lane == 0) arrive_leader(acce_bar(acc));
       if (threadIdx.x == 0) {
         if (etile == 0) trace_cta(prm, 2);
-        trace_event(tsm, 5, etile++);
+        trace_event(tsm, 5, etile++ - tbase / 32u);
       }
       if (++acc == A) { acc = 0; aph ^= 1; }
       const int p = ti.p0 + row;

@@ -127,6 +127,18 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// CTA-pair form: the tile lands in this CTA's shared memory (dst), and the transaction
+// bytes are counted on `bar_cluster`, a shared::cluster address that may name the
+// barrier in the peer CTA of the pair (no multicast: one destination, one source).
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void* tmap, uint32_t bar_cluster,
+                                                 int x, int y, int z, uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z), "l"(cache_hint)
+      : "memory");
+}
+
 // Plain (untiled) bulk copy global -> shared; both addresses 16-B aligned,
 // size a multiple of 16.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
@@ -384,31 +396,6 @@ __device__ __forceinline__ void tc_commit_2cta(uint32_t bar) {
       : "memory");
 }
 // try_wait that acquires at cluster scope (for phases completed by the peer CTA).
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait_bounded_cluster(uint32_t bar, uint32_t parity,
-                                                          volatile int* abort_flag, int* status,
-                                                          int code, uint64_t timeout_ns) {
-  const uint64_t t0 = global_timer_ns();
-  while (true) {
-    if (mbar_try_wait_cluster(bar, parity, 1000000u)) return true;
-    if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > timeout_ns) {
-      *abort_flag = 1;
-      if (status) atomicCAS(status, 0, code);
-      return false;
-    }
-  }
-}
 
 // Named barrier among a subset of warps (id 1..15).
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads) {

@@ -108,6 +108,25 @@ int encode_operand_map(CUtensorMap* m, const void* ptr, long long rows, long lon
   return NVFP4_OK;
 }
 
+// Scale-factor map of one operand's permuted scales (L, ceil(mn/128), K/64 atoms of 512
+// bytes) seen as 8-byte elements: row = one 128-row block, box = the KB atoms of one
+// k-stage of `blocks` consecutive blocks.  Out-of-range blocks and atoms read as zero.
+int encode_sf_map(CUtensorMap* m, const void* ptr, long long mn, long long k, long long batch,
+                  int kb, int blocks) {
+  const long long rk = (k + 63) / 64, rest = (mn + 127) / 128;
+  cuuint64_t dims[3] = {(cuuint64_t)(rk * 64), (cuuint64_t)rest, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(rk * kAtomBytes), (cuuint64_t)(rest * rk * kAtomBytes)};
+  cuuint32_t box[3] = {(cuuint32_t)(kb * 64), (cuuint32_t)blocks, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_INT64, 3, const_cast<void*>(ptr), dims, strides,
+                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(NVFP4_ERR_DRIVER, "cuTensorMapEncodeTiled (scales) failed (%d) mn=%lld k=%lld",
+                (int)r, mn, k);
+  return NVFP4_OK;
+}
+
 // Per-thread memo of recent operand maps: a repeated call on the same buffers skips
 // the driver encode (about a microsecond each).  The key covers every input of the
 // encoding, so a hit is exactly the map the driver would build again.
@@ -115,9 +134,10 @@ struct MapKey {
   const void* ptr;
   long long rows, kbytes, batch;
   int box_rows, box_inner;
+  int kind;  // 0 operand map, 1 scale-factor map
   bool operator==(const MapKey& o) const {
     return ptr == o.ptr && rows == o.rows && kbytes == o.kbytes && batch == o.batch &&
-           box_rows == o.box_rows && box_inner == o.box_inner;
+           box_rows == o.box_rows && box_inner == o.box_inner && kind == o.kind;
   }
 };
 struct MapEntry {
@@ -129,15 +149,17 @@ constexpr int kMapCache = 16;
 thread_local MapEntry g_map_cache[kMapCache];
 thread_local int g_map_next = 0;
 
-int cached_operand_map(CUtensorMap* m, const void* ptr, long long rows, long long kbytes,
-                       long long batch, int box_rows, int box_inner) {
-  const MapKey key{ptr, rows, kbytes, batch, box_rows, box_inner};
+int cached_map(CUtensorMap* m, int kind, const void* ptr, long long rows, long long kbytes,
+               long long batch, int box_rows, int box_inner) {
+  const MapKey key{ptr, rows, kbytes, batch, box_rows, box_inner, kind};
   for (int i = 0; i < kMapCache; ++i)
     if (g_map_cache[i].valid && g_map_cache[i].key == key) {
       *m = g_map_cache[i].map;
       return NVFP4_OK;
     }
-  int rc = encode_operand_map(m, ptr, rows, kbytes, batch, box_rows, box_inner);
+  // (scale maps: rows = mn, kbytes = k, box_rows = blocks, box_inner = KB)
+  int rc = kind == 0 ? encode_operand_map(m, ptr, rows, kbytes, batch, box_rows, box_inner)
+                     : encode_sf_map(m, ptr, rows, kbytes, batch, box_inner, box_rows);
   if (rc) return rc;
   MapEntry& e = g_map_cache[g_map_next];
   g_map_next = (g_map_next + 1) % kMapCache;
@@ -179,7 +201,8 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 }
 
 template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false>
-int launch(const CUtensorMap& tp, const CUtensorMap& tq, const GemmParams& prm, int grid,
+int launch(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tsp,
+           const CUtensorMap& tsq, const GemmParams& prm, int grid,
            cudaStream_t stream) {
   using C_ = Cfg<BN, KB, CTA2>;
   auto kern = nvfp4_gemm_kernel<GROUPED, SWAP, BN, KB, CTA2>;
@@ -198,7 +221,7 @@ int launch(const CUtensorMap& tp, const CUtensorMap& tq, const GemmParams& prm, 
     attr_done[dev] = true;
   }
   cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kNumThreads), smem, stream,
-                             CTA2 ? 2 : 1, tp, tq, prm);
+                             CTA2 ? 2 : 1, tp, tq, tsp, tsq, prm);
   if (e != cudaSuccess) return cuda_fail(e, "nvfp4_gemm_kernel launch");
   return NVFP4_OK;
 }
@@ -240,10 +263,14 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   const int p_rows = SWAP ? n : m;
   const int q_rows = SWAP ? m : n;
   const long long kbytes = k / 2;
-  CUtensorMap tp, tq;
-  int rc = cached_operand_map(&tp, P, p_rows, kbytes, l, kBM, KB * 32);
+  CUtensorMap tp, tq, tsp, tsq;
+  int rc = cached_map(&tp, 0, P, p_rows, kbytes, l, kBM, KB * 32);
   if (rc) return rc;
-  rc = cached_operand_map(&tq, Q, q_rows, kbytes, l, CTA2 ? BN / 2 : BN, KB * 32);
+  rc = cached_map(&tq, 0, Q, q_rows, kbytes, l, CTA2 ? BN / 2 : BN, KB * 32);
+  if (rc) return rc;
+  rc = cached_map(&tsp, 1, sfP, p_rows, k, l, 1, KB);
+  if (rc) return rc;
+  rc = cached_map(&tsq, 1, sfQ, q_rows, k, l, Cfg<BN, KB, CTA2>::kSfqAtoms, KB);
   if (rc) return rc;
   GemmParams prm;
   std::memset(&prm, 0, sizeof(prm));
@@ -280,7 +307,7 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   } else if (grid > prm.total_tiles) {
     grid = prm.total_tiles;
   }
-  return launch<false, SWAP, BN, KB, CTA2>(tp, tq, prm, grid, stream);
+  return launch<false, SWAP, BN, KB, CTA2>(tp, tq, tsp, tsq, prm, grid, stream);
 }
 
 // ------------------------------------------------------------------ grouped GEMM
@@ -417,7 +444,8 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   prm.trace = opt ? reinterpret_cast<unsigned long long*>(opt->trace) : nullptr;
   int grid = st->num_sms;
   if (opt && opt->max_ctas > 0 && opt->max_ctas < grid) grid = opt->max_ctas;
-  return launch<true, true, BN, KB>(tp, tq, prm, grid, stream);
+  // (the grouped kernel copies scales with plain bulk copies: the scale maps are unused)
+  return launch<true, true, BN, KB>(tp, tq, tp, tq, prm, grid, stream);
 }
 
 }  // namespace

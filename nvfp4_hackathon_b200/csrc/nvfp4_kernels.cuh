@@ -12,17 +12,17 @@
 // "swap" P = B, Q = A and C[m, n] = D[n, m], which puts a skinny M (decode-like
 // shapes, small MoE groups) on the flexible N side of the MMA.
 //
-// Roles (19 warps):
+// Roles (20 warps):
 //   warps 0-7   epilogue: warp w drains TMEM lanes 32*(w%4).. and column half w/4 of the
 //               accumulator into registers as fp16, releases the accumulator, then stores
 //               to global while the next tile's MMAs already run
-//   warps 8-9   producers (alternating k-stages): TMA loads of the P and Q tiles (128-byte
+//   warps 8-10  producers (k-steps round-robin): TMA loads of the P and Q tiles (128-byte
 //               swizzle) into a ring of kStages stages, and plain bulk copies of the scale
 //               atoms into their own ring of slots, kSfLead k-steps ahead of the operands
-//   warp 10     TMEM owner and MMA issuer: per k-step it waits for the stage's operand
+//   warp 11     TMEM owner and MMA issuer: per k-step it waits for the stage's operand
 //               tiles (full) and scales (sf_full), issues tcgen05.mma kind::mxf4nvf4
 //               (K = 64 per instruction) and one tcgen05.commit to release the stage.
-//   warps 11-18 scale warps, two groups of four (group g serves k-steps j with j % 2 == g):
+//   warps 12-19 scale warps, two groups of four (group g serves k-steps j with j % 2 == g):
 //               each warp moves the step's scale atoms from their slot into its own 32
 //               TMEM lanes with ld.shared + tcgen05.st, once the step's TMEM scale buffer
 //               is free (the stage's previous MMAs committed).  tcgen05.cp would run in
@@ -50,10 +50,13 @@ namespace nvfp4 {
 constexpr int kBM = 128;            // MMA M (rows of P per tile)
 constexpr int kAtomBytes = 512;     // one scale-factor atom: 128 rows x 4 K-vectors
 constexpr int kEpiWarps = 8;
-constexpr int kProducerWarp = 8;   // warps 8 and 9: stage issue alternates between them
-constexpr int kNumProducers = 2;
-constexpr int kMmaWarp = 10;
-constexpr int kFirstSfWarp = 11;
+// Producer warps 8..10 take the k-steps round-robin: a TMA instruction occupies its issuing
+// thread for ~160 cycles, so one thread issues a stage (2 tensor + up to 3 bulk copies)
+// only every ~0.4 us.
+constexpr int kProducerWarp = 8;
+constexpr int kNumProducers = 3;  // (a 21st warp would cost the block its 96-register budget)
+constexpr int kMmaWarp = kProducerWarp + kNumProducers;
+constexpr int kFirstSfWarp = kMmaWarp + 1;
 constexpr int kSfGroups = 2;        // groups of 4 scale warps; group g serves k-steps j % 2 == g
 constexpr int kNumThreads = 32 * (kFirstSfWarp + 4 * kSfGroups);
 constexpr int kMaxDynamicSmem = 232448;     // opt-in dynamic shared memory per CTA on sm_100
@@ -106,7 +109,9 @@ struct Cfg {
   static constexpr int kBarrierBytes = 8 * kNumBars + 16;
   static constexpr int kSmemBytes =
       1024 + kStages * kStageBytes + kSfSlots * kSfSlotBytes + kBarrierBytes;
-  static_assert(kStages >= 2, "need at least two stages");
+  // a producer's previous step j - kNumProducers must imply that step j - 2 S was consumed,
+  // or its parity wait on the empty barrier for step j - S could alias
+  static_assert(kStages >= kNumProducers, "need at least one stage per producer warp");
   static_assert(kColsNeeded <= 512, "TMEM budget exceeded");
   static_assert(kSfSlots <= 32, "slot bookkeeping uses 32-bit masks");
   static_assert(kSmemBytes + 1024 <= kMaxDynamicSmem, "shared memory budget exceeded (incl. trace)");
@@ -250,6 +255,7 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtenso
 template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
 nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constant__ CUtensorMap tm_q,
+                  const __grid_constant__ CUtensorMap tm_sfp, const __grid_constant__ CUtensorMap tm_sfq,
                   const GemmParams prm) {
   static_assert(!(CTA2 && GROUPED), "CTA pairs are used for the dense GEMM only");
   using C_ = Cfg<BN, KB, CTA2>;
@@ -322,6 +328,8 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   if (warp >= kProducerWarp && warp < kProducerWarp + kNumProducers && lane == 0 && !GROUPED) {
     prefetch_tmap(&tm_p);
     prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_sfp);
+    prefetch_tmap(&tm_sfq);
   }
   if (warp == kMmaWarp) {
     if (CTA2) {
@@ -397,9 +405,20 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           mbar_arrive(bar);
           return;
         }
+        const uint32_t dst = base + slot_off(sl);
+        if constexpr (!GROUPED) {
+          // two tensor loads (one per operand's scale blocks; out-of-range atoms read as
+          // zero and are ignored): a tensor load costs the issuing thread ~50 cycles, a
+          // plain bulk copy ~115
+          mbar_arrive_expect_tx(bar, C_::kSfSlotBytes);
+          tma_load_3d(dst, &tm_sfp, bar, c.kt * KB * 64, c.ti.p0 >> 7, c.ti.l, pol_keep);
+          tma_load_3d(dst + kOffSfq, &tm_sfq, bar, c.kt * KB * 64, c.ti.q0 >> 7, c.ti.l, pol_keep);
+          sf_issued |= 1u << sl;
+          sf_par = (sf_par & ~(1u << sl)) | (slph << sl);
+          return;
+        }
         const uint32_t sf_bytes = k_blocks(c.ti, c.kt) * kAtomBytes;
         const int nq = q_atoms(c.ti);
-        const uint32_t dst = base + slot_off(sl);
         mbar_arrive_expect_tx(bar, sf_bytes * (1 + nq));
         bulk_load(dst, c.ti.sf_p + ((long long)(c.ti.p0 >> 7) * c.ti.rk + c.kt * KB) * kAtomBytes,
                   sf_bytes, bar, pol_keep);
@@ -417,7 +436,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         cur_next(sfc);
       };
       // scale atoms of steps 0 .. LEAD-1 go out first (their slots are fresh)
-      for (int j = 0; j < LEAD; ++j) sf_step((j & 1) == (int)pid);
+      for (int j = 0; j < LEAD; ++j) sf_step(j % kNumProducers == (int)pid);
       for (int t = work0; t < total && ok; t += work_step) {
         TileInfo ti;
         decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, t, ti);
@@ -427,7 +446,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           last_map = ti.map_p;
         }
         for (int kt = 0; kt < ti.num_kt; ++kt, ++gstep) {
-          const bool mine = (gstep & 1) == pid;
+          const bool mine = gstep % kNumProducers == pid;
           if (mine) {
             // stage s free: the MMAs of step gstep - S are done (and with them every read
             // of the scale slot step gstep + LEAD reuses)

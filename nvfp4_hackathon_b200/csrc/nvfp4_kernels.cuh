@@ -330,6 +330,20 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_sfp);
     prefetch_tmap(&tm_sfq);
+    // Pull this CTA's first k-stages into L2 while the previous kernel finishes: an L2
+    // prefetch is safe before the wait on that kernel even if it writes these inputs
+    // (L2 is the point of coherence, nothing lands in this SM).  Dense only: the grouped
+    // schedule is itself written by the preceding prep kernel.
+    if (work0 < prm.total_tiles) {
+      TileInfo ti;
+      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, work0, ti);
+      for (int kt = warp - kProducerWarp; kt < S && kt < ti.num_kt; kt += kNumProducers) {
+        tma_prefetch_l2_3d(&tm_p, kt * C_::kBKBytes, ti.p0, ti.l);
+        tma_prefetch_l2_3d(&tm_q, kt * C_::kBKBytes, ti.q0 + (int)crank * C_::kQRows, ti.l);
+        tma_prefetch_l2_3d(&tm_sfp, kt * KB * 64, ti.p0 >> 7, ti.l);
+        tma_prefetch_l2_3d(&tm_sfq, kt * KB * 64, ti.q0 >> 7, ti.l);
+      }
+    }
   }
   if (warp == kMmaWarp) {
     if (CTA2) {

@@ -113,6 +113,25 @@ int nvfp4_grouped_gemm_ex(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev
                           size_t workspace_bytes, void* stream, const nvfp4_options* opt);
 
 /*
+ * Quantise x to NVFP4 on the GPU: the inputs the GEMMs take, computed from real values.
+ * Replaces the host-side generation steps of the reference (kernels/gemm/reference.py:86-150:
+ * per-16-element amax / 6 -> e4m3 scale, nearest e2m1 code, to_blocked scale permutation),
+ * which the reference runs with torch ops before the timed GEMM.
+ *   x        : (l, rows, k) contiguous, dtype NVFP4_DTYPE_F32 / _F16 / _BF16
+ *   codes    : (l, rows, k/2) bytes, element 2i in the low nibble
+ *   sf_perm  : (l, ceil(rows/128), k/64, 512) bytes, the permuted layout (padding rows 0)
+ *   sf_plain : NULL, or (l, rows, k/16) bytes
+ * Rounding: scale = e4m3(amax / 6) to nearest even (out of range -> NaN), code = nearest
+ * e2m1 of |x| / scale clamped to 6, ties to the even code.  Requirements: k % 64 == 0;
+ * x, codes, sf_perm 16-byte aligned.
+ */
+#define NVFP4_DTYPE_F32 0
+#define NVFP4_DTYPE_F16 1
+#define NVFP4_DTYPE_BF16 2
+int nvfp4_quantize(const void* x, int dtype, int rows, int k, int l, void* codes, void* sf_perm,
+                   void* sf_plain, void* stream);
+
+/*
  * Grouped NVFP4 GEMM that allocates nothing.  No counterpart in the reference;
  * it is for callers that must not allocate device memory at call time, such as
  * code running inside a pre-planned memory pool or a host runtime that owns

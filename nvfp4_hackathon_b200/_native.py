@@ -44,6 +44,7 @@ EXPORTED = (
     "nvfp4_grouped_gemm",
     "nvfp4_grouped_gemm_ex",
     "nvfp4_grouped_gemm_noalloc",
+    "nvfp4_quantize",
 )
 
 
@@ -105,6 +106,7 @@ def _load_slow() -> ctypes.CDLL:
         lib.nvfp4_grouped_gemm_ex.argtypes = [vp, vp, vp, i, vp, sz, vp,
                                               ctypes.POINTER(Nvfp4Options)]
         lib.nvfp4_grouped_gemm_noalloc.argtypes = [vp, vp, vp, i, vp]
+        lib.nvfp4_quantize.argtypes = [vp, i, i, i, i, vp, vp, vp, vp]
         for name in EXPORTED:
             getattr(lib, name)  # AttributeError here means a stale build
         _lib = lib

@@ -10,7 +10,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 ROOT = os.path.dirname(PKG)
 SOURCES = ["nvfp4_capi.cu"]
-HEADERS = ["nvfp4_kernels.cuh", "ptx_sm100.cuh"]
+HEADERS = ["nvfp4_kernels.cuh", "nvfp4_quant.cuh", "ptx_sm100.cuh"]
 OUT = os.path.join(PKG, "libnvfp4_b200.so")
 
 

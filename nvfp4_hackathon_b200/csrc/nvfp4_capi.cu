@@ -17,6 +17,7 @@
 #include <utility>
 
 #include "nvfp4_kernels.cuh"
+#include "nvfp4_quant.cuh"
 #include "../../include/nvfp4_b200.h"
 
 using namespace nvfp4;
@@ -572,6 +573,32 @@ int nvfp4_grouped_gemm(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev,
                        void* stream) {
   return nvfp4_grouped_gemm_ex(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, workspace_bytes,
                                stream, nullptr);
+}
+
+int nvfp4_quantize(const void* x, int dtype, int rows, int k, int l, void* codes, void* sf_perm,
+                   void* sf_plain, void* stream) {
+  if (!x || !codes || !sf_perm) return fail(NVFP4_ERR_INVALID_ARG, "null pointer");
+  if (rows <= 0 || l <= 0 || k <= 0) return fail(NVFP4_ERR_INVALID_ARG, "non-positive size");
+  if (k % 64) return fail(NVFP4_ERR_UNSUPPORTED, "k must be a multiple of 64 (got %d)", k);
+  if (dtype < kQuantF32 || dtype > kQuantBF16) return fail(NVFP4_ERR_INVALID_ARG, "dtype %d", dtype);
+  if (!aligned16(x) || !aligned16(codes) || !aligned16(sf_perm))
+    return fail(NVFP4_ERR_ALIGNMENT, "x, codes and sf_perm must be 16-byte aligned");
+  const int rm = (rows + 127) / 128;
+  if (rm > 65535 || l > 65535) return fail(NVFP4_ERR_UNSUPPORTED, "too many rows or batches");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const dim3 grid((k / 64 + kQuantAtoms - 1) / kQuantAtoms, rm, l);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* c8 = static_cast<uint8_t*>(codes);
+  auto* sp = static_cast<uint8_t*>(sf_perm);
+  auto* pl = static_cast<uint8_t*>(sf_plain);
+  if (dtype == kQuantF32) nvfp4_quantize_kernel<kQuantF32><<<grid, 256, 0, s>>>(x, rows, k, c8, sp, pl);
+  else if (dtype == kQuantF16) nvfp4_quantize_kernel<kQuantF16><<<grid, 256, 0, s>>>(x, rows, k, c8, sp, pl);
+  else nvfp4_quantize_kernel<kQuantBF16><<<grid, 256, 0, s>>>(x, rows, k, c8, sp, pl);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "nvfp4_quantize_kernel launch");
+  return NVFP4_OK;
 }
 
 }  // extern "C"

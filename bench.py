@@ -398,7 +398,8 @@ def bench_ours(args):
             roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(fp4_peak, 1),
                     "unit": "TFLOP/s", "frac": round(achieved / fp4_peak, 4),
                     "peak_source": f"4 x {peak_src} bf16_tflops (dense fp4 rate = 4x bf16 on B200)"}
-        roof["traffic"] = profile_traffic(f"nvfp4_gemm_{args.config}")
+        tag = "nvfp4_gemm_" if wl.kind.startswith("dense") else "nvfp4_grouped_"
+        roof["traffic"] = profile_traffic(tag + args.config)
         roof["algorithmic_bytes_per_launch"] = wl.bytes
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,

@@ -45,3 +45,36 @@ def quantize(x: torch.Tensor, stream=None, plain: bool = True):
     sf_v = flat.view(torch.float8_e4m3fn).permute(1, 2, 0) if plain else None
     perm_v = perm.view(torch.float8_e4m3fn).permute(3, 4, 1, 5, 2, 0)
     return codes_v, sf_v, perm_v
+
+
+def _main():
+    """Time the quantiser: python -m nvfp4_hackathon_b200.quantize --rows 8192 --k 8192."""
+    import argparse
+    import json
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--rows", type=int, default=8192)
+    ap.add_argument("--k", type=int, default=8192)
+    ap.add_argument("--dtype", default="bf16", choices=["f32", "f16", "bf16"])
+    ap.add_argument("--reps", type=int, default=20)
+    args = ap.parse_args()
+    dt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[args.dtype]
+    # three inputs so consecutive calls do not find their input in L2
+    xs = [torch.randn((args.rows, args.k), device="cuda", dtype=dt) for _ in range(3)]
+    for x in xs:
+        quantize(x, plain=False)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record()
+    for i in range(args.reps):
+        quantize(xs[i % 3], plain=False)
+    ev[1].record()
+    torch.cuda.synchronize()
+    us = ev[0].elapsed_time(ev[1]) * 1e3 / args.reps
+    nbytes = args.rows * args.k * (xs[0].element_size() + 0.5 + 1.0 / 16)
+    print(json.dumps({"rows": args.rows, "k": args.k, "dtype": args.dtype, "us_per_call": round(us, 2),
+                      "gb_per_s": round(nbytes / us / 1e3, 1)}))
+
+
+if __name__ == "__main__":
+    _main()

@@ -61,6 +61,9 @@ typedef struct nvfp4_options {
                                      followed by 4 stamps per CTA (entry, start, first tile, exit) */
   int stage_k;                    /* 0 = auto; 128 or 256 K elements per pipeline stage */
   int cta_pair;                   /* 0 = auto, 1 = off, 2 = M=256 tiles on a CTA pair (cta_group::2) */
+  int stream_k;                   /* dense: 0 = auto (when tiles < SMs), 1 = off, 2 = on.  Stream-K
+                                     keeps a small per-stream workspace (flags + fp32 partials,
+                                     ~16 MiB) allocated on first use outside stream capture */
 } nvfp4_options;
 
 /* Human-readable message for the last error returned on this thread. */

@@ -8,6 +8,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -15,6 +16,7 @@
 #include <mutex>
 #include <string>
 #include <utility>
+#include <vector>
 
 #include "nvfp4_kernels.cuh"
 #include "nvfp4_quant.cuh"
@@ -174,25 +176,31 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // Launch with programmatic stream serialization: the kernel may start while the
 // previous kernel on the stream finishes; it calls griddepcontrol.wait before it
-// touches global memory.
+// touches global memory.  `coop`: cooperative launch (all CTAs co-resident), for grids
+// whose CTAs wait on one another.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                       int cluster, Args&&... args) {
+                       int cluster, bool coop, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[3];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   int n = 1;
   if (cluster > 1) {
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = cluster;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = 1;
-    n = 2;
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (coop) {
+    attr[n].id = cudaLaunchAttributeCooperative;
+    attr[n].val.cooperative = 1;
+    ++n;
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
@@ -222,7 +230,7 @@ int launch(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tsp,
     attr_done[dev] = true;
   }
   cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kNumThreads), smem, stream,
-                             CTA2 ? 2 : 1, tp, tq, tsp, tsq, prm);
+                             CTA2 ? 2 : 1, prm.sk_ktn > 0, tp, tq, tsp, tsq, prm);
   if (e != cudaSuccess) return cuda_fail(e, "nvfp4_gemm_kernel launch");
   return NVFP4_OK;
 }
@@ -250,6 +258,55 @@ DenseChoice choose_dense(int m, int n, int k, const nvfp4_options* opt) {
     if (opt->tile_n > 0) c.bn = opt->tile_n;
   }
   return c;
+}
+
+// Stream-K workspace of one (device, stream): a flag per CTA (up to kSkMaxCtas) and one
+// fp32 partial tile (128 x BN) per CTA in kSkSlotsBytes.  Allocated on first use and kept;
+// none is allocated while the stream is being captured into a graph (the call then runs
+// without stream-K).
+constexpr int kSkMaxCtas = 1024;
+constexpr size_t kSkSlotsBytes = 16u << 20;
+struct SkWorkspace {
+  int dev;
+  cudaStream_t stream;
+  void* ptr;
+};
+std::mutex g_sk_mu;
+std::vector<SkWorkspace> g_sk;
+
+void* sk_workspace(int dev, cudaStream_t stream) {
+  std::lock_guard<std::mutex> lk(g_sk_mu);
+  for (const SkWorkspace& w : g_sk)
+    if (w.dev == dev && w.stream == stream) return w.ptr;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  void* p = nullptr;
+  const size_t bytes = kSkMaxCtas * sizeof(unsigned) + kSkSlotsBytes;
+  if (cap == cudaStreamCaptureStatusNone) {
+    if (cudaMalloc(&p, bytes) != cudaSuccess || cudaMemset(p, 0, kSkMaxCtas * sizeof(unsigned)) != cudaSuccess) {
+      if (p) cudaFree(p);
+      cudaGetLastError();
+      return nullptr;
+    }
+  } else {
+    // A stream being captured into a graph: a one-time allocation, outside the capture
+    // (relaxed mode for this thread only), that the graph's launches keep using.  The
+    // flags need no clearing: the kernel clears each CTA's flag itself, and a published
+    // flag holds kSkPublished, which fresh memory does not.
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    const cudaError_t e = cudaMalloc(&p, bytes);
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+  }
+  g_sk.push_back({dev, stream, p});
+  return p;
 }
 
 template <bool SWAP, int BN, int KB, bool CTA2 = false>
@@ -307,6 +364,37 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
     grid = 2 * pairs;
   } else if (grid > prm.total_tiles) {
     grid = prm.total_tiles;
+  }
+  // Stream-K when the tiles would leave most SMs idle (skinny M, few tiles, long K): every
+  // CTA takes an equal share of all k-steps, and a split tile's fp32 partials meet in the
+  // CTA holding its k-step 0.  The reduction costs about one L2 round trip per piece, so
+  // auto mode needs tiles <= SMs / 2 and >= 16 k-steps per tile, and splits a tile into
+  // 2 pieces (>= 48 k-steps) or 3 (B200, M = 128: 128 x 7168 x 16384 36 -> 27 us,
+  // 128 x 1536 x 7168 17.7 -> 15.3 us; shorter K or more pieces lose).  stream_k = 2 uses
+  // every SM (or max_ctas).  BN <= 128 (the fp32 partial fits in registers); no CTA pairs.
+  const int ktn = (k + KB * 64 - 1) / (KB * 64);
+  const int sk_opt = opt ? opt->stream_k : 0;
+  const bool sk_auto = sk_opt == 0 && 2 * prm.total_tiles <= st->num_sms && ktn >= 16;
+  if (!CTA2 && BN <= 128 && ktn >= 2 && (sk_opt == 2 || sk_auto)) {
+    int g = st->num_sms;
+    if (opt && opt->max_ctas > 0 && opt->max_ctas < g) g = opt->max_ctas;
+    if (sk_auto) g = std::min(g, (ktn >= 48 ? 2 : 3) * prm.total_tiles);
+    if ((long long)prm.total_tiles * ktn < g) g = prm.total_tiles * ktn;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    void* ws = (g <= kSkMaxCtas && (size_t)g * BN * 128 * sizeof(float) <= kSkSlotsBytes &&
+                (long long)prm.total_tiles * ktn < 0x7fffffffLL)
+                   ? sk_workspace(dev, stream) : nullptr;
+    if (ws && g > prm.total_tiles) {
+      prm.sk_ktn = ktn;
+      prm.sk_flags = static_cast<unsigned*>(ws);
+      prm.sk_slots = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kSkMaxCtas * sizeof(unsigned));
+      rc = launch<false, SWAP, BN, KB, CTA2>(tp, tq, tsp, tsq, prm, g, stream);
+      if (rc == NVFP4_OK) return rc;
+      // (a cooperative launch the device refuses: run the plain schedule instead)
+      cudaGetLastError();
+      prm.sk_ktn = 0;
+    }
   }
   return launch<false, SWAP, BN, KB, CTA2>(tp, tq, tsp, tsq, prm, grid, stream);
 }
@@ -429,7 +517,7 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   int* prefix = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) +
                                        align_up((size_t)G * 2 * sizeof(CUtensorMap), 256));
   const int threads = ((G + 31) / 32) * 32;
-  cudaError_t e = launch_pdl(nvfp4_grouped_prep, dim3(1), dim3(threads), 0, stream, 1, tp, tq, sizes,
+  cudaError_t e = launch_pdl(nvfp4_grouped_prep, dim3(1), dim3(threads), 0, stream, 1, false, tp, tq, sizes,
                              reinterpret_cast<const unsigned long long*>(abc),
                              reinterpret_cast<const unsigned long long*>(sfs), G, maps, prefix, BN,
                              st->status);

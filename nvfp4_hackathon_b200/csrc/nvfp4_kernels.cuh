@@ -138,6 +138,11 @@ struct GemmParams {
   const unsigned long long* sfs;  // G x 2: sfa (permuted), sfb (permuted)
   const CUtensorMap* maps;      // G x 2: [P map = B_g, Q map = A_g]
   const int* tile_prefix;       // G + 1 running tile counts
+  // stream-K (dense only): when sk_ktn > 0 every CTA takes an equal contiguous range of
+  // the total_tiles x sk_ktn k-steps; partial tiles meet through sk_slots / sk_flags
+  int sk_ktn;
+  float* sk_slots;              // per CTA: BN/4 x 128 float4 (column group major)
+  unsigned* sk_flags;           // per CTA: kSkPublished while its partial is published
   // control
   int* status;
   unsigned long long timeout_ns;
@@ -191,6 +196,45 @@ struct TileInfo {
   int rk;                // 64-wide K blocks (atoms per 128-row block)
   int num_kt;            // K stages (KB * 64 wide)
 };
+
+constexpr unsigned kSkPublished = 0x9E3779B9u;  // stream-K flag value of a published partial
+
+// A CTA's work is a list of segments: k-steps [kt0, kt1) of tile t (kt1 is clipped to the
+// tile's k-steps).  Without stream-K a segment is a whole tile, CTA w taking tiles w,
+// w + step, ...; with stream-K CTA w takes global k-steps [start(w), start(w + 1)) of the
+// tiles laid end to end, which is at most a tail, whole tiles and a head.
+struct Seg {
+  int t, kt0, kt1;
+};
+__device__ __forceinline__ int sk_start(const GemmParams& prm, int w, int nwork) {
+  return (int)((long long)prm.total_tiles * prm.sk_ktn * w / nwork);
+}
+__device__ __forceinline__ bool seg_first(const GemmParams& prm, int total, int w, int step, Seg& sg) {
+  if (prm.sk_ktn) {
+    const int b = sk_start(prm, w, step), e = sk_start(prm, w + 1, step);
+    if (b >= e) return false;
+    sg.t = b / prm.sk_ktn;
+    sg.kt0 = b - sg.t * prm.sk_ktn;
+    sg.kt1 = min(prm.sk_ktn, e - sg.t * prm.sk_ktn);
+    return true;
+  }
+  sg.t = w;
+  sg.kt0 = 0;
+  sg.kt1 = 0x7fffffff;
+  return w < total;
+}
+__device__ __forceinline__ bool seg_next(const GemmParams& prm, int total, int w, int step, Seg& sg) {
+  if (prm.sk_ktn) {
+    const int e = sk_start(prm, w + 1, step);
+    sg.t += 1;
+    if (sg.t * prm.sk_ktn >= e) return false;
+    sg.kt0 = 0;
+    sg.kt1 = min(prm.sk_ktn, e - sg.t * prm.sk_ktn);
+    return true;
+  }
+  sg.t += step;
+  return sg.t < total;
+}
 
 template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false>
 __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtensorMap* tm_p,
@@ -334,10 +378,12 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     // prefetch is safe before the wait on that kernel even if it writes these inputs
     // (L2 is the point of coherence, nothing lands in this SM).  Dense only: the grouped
     // schedule is itself written by the preceding prep kernel.
-    if (work0 < prm.total_tiles) {
+    Seg sg0;
+    if (seg_first(prm, prm.total_tiles, work0, work_step, sg0)) {
       TileInfo ti;
-      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, work0, ti);
-      for (int kt = warp - kProducerWarp; kt < S && kt < ti.num_kt; kt += kNumProducers) {
+      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg0.t, ti);
+      const int kte = min(sg0.kt1, ti.num_kt);
+      for (int kt = sg0.kt0 + (warp - kProducerWarp); kt < sg0.kt0 + S && kt < kte; kt += kNumProducers) {
         tma_prefetch_l2_3d(&tm_p, kt * C_::kBKBytes, ti.p0, ti.l);
         tma_prefetch_l2_3d(&tm_q, kt * C_::kBKBytes, ti.q0 + (int)crank * C_::kQRows, ti.l);
         tma_prefetch_l2_3d(&tm_sfp, kt * KB * 64, ti.p0 >> 7, ti.l);
@@ -364,6 +410,9 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   // that kernel has completed.
   pdl_wait_prior_grid();
   if (threadIdx.x == 0) trace_cta(prm, 1);
+  // stream-K: this CTA's partial is not published yet (the owner of a tile also clears the
+  // flags it consumed; this covers a launch that ended early)
+  if (!GROUPED && prm.sk_ktn && threadIdx.x == 0) prm.sk_flags[blockIdx.x] = 0u;
 
   const int total = GROUPED ? __ldg(prm.tile_prefix + prm.G) : prm.total_tiles;
   const uint64_t tmo = prm.timeout_ns;
@@ -396,20 +445,26 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       // Cursor over this CTA's k-steps (tile, k-stage) LEAD steps ahead of the operand
       // loads: the scale atoms of that step go into its slot of the scale ring.
       struct Cursor {
-        int t, kt;
+        Seg sg;
+        int kt, kte;
+        bool valid;
         TileInfo ti;
       };
+      auto cur_load = [&](Cursor& c) {
+        if (!c.valid) return;
+        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, c.sg.t, c.ti);
+        c.kt = c.sg.kt0;
+        c.kte = min(c.sg.kt1, c.ti.num_kt);
+      };
       auto cur_next = [&](Cursor& c) {
-        if (++c.kt == c.ti.num_kt) {
-          c.kt = 0;
-          c.t += work_step;
-          if (c.t < total) decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, c.t, c.ti);
+        if (++c.kt == c.kte) {
+          c.valid = seg_next(prm, total, work0, work_step, c.sg);
+          cur_load(c);
         }
       };
       Cursor sfc;
-      sfc.t = work0;
-      sfc.kt = 0;
-      if (sfc.t < total) decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sfc.t, sfc.ti);
+      sfc.valid = seg_first(prm, total, work0, work_step, sfc.sg);
+      cur_load(sfc);
       int sl = 0;
       uint32_t slph = 0;
       uint32_t sf_issued = 0, sf_par = 0;
@@ -444,22 +499,25 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         sf_par = (sf_par & ~(1u << sl)) | (slph << sl);
       };
       auto sf_step = [&](bool mine) {  // the cursor's step: issue if it is ours, then advance
-        if (sfc.t >= total) return;
+        if (!sfc.valid) return;
         if (mine) issue_sf(sfc);
         if (++sl == NS) { sl = 0; slph ^= 1; }
         cur_next(sfc);
       };
       // scale atoms of steps 0 .. LEAD-1 go out first (their slots are fresh)
       for (int j = 0; j < LEAD; ++j) sf_step(j % kNumProducers == (int)pid);
-      for (int t = work0; t < total && ok; t += work_step) {
+      Seg sg;
+      for (bool more = seg_first(prm, total, work0, work_step, sg); more && ok;
+           more = seg_next(prm, total, work0, work_step, sg)) {
         TileInfo ti;
-        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, t, ti);
+        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg.t, ti);
         if (GROUPED && ti.map_p != last_map) {
           tmap_fence_acquire(ti.map_p);
           tmap_fence_acquire(ti.map_q);
           last_map = ti.map_p;
         }
-        for (int kt = 0; kt < ti.num_kt; ++kt, ++gstep) {
+        const int kte = min(sg.kt1, ti.num_kt);
+        for (int kt = sg.kt0; kt < kte; ++kt, ++gstep) {
           const bool mine = gstep % kNumProducers == pid;
           if (mine) {
             // stage s free: the MMAs of step gstep - S are done (and with them every read
@@ -513,9 +571,12 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       int s = 0;
       uint32_t ph = 0;
       uint32_t step = 0;
-      for (int t = work0; t < total && ok; t += work_step) {
+      Seg sg;
+      for (bool more = seg_first(prm, total, work0, work_step, sg); more && ok;
+           more = seg_next(prm, total, work0, work_step, sg)) {
         TileInfo ti;
-        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, t, ti);
+        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg.t, ti);
+        const int kte = min(sg.kt1, ti.num_kt);
         // A pair splits the instruction's N in halves between the two CTAs' shared memory,
         // so it always issues N = BN (each CTA staged BN/2 rows; rows past the edge are zero).
         int n_mma = ti.q_rows - ti.q0;
@@ -531,7 +592,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
             !mbar_wait_bounded(acce_bar(acc), aph ^ 1, abort_flag, prm.status, kStatusTimeoutMma,
                                tmo)) { ok = false; break; }
         tc_fence_after();
-        for (int kt = 0; kt < ti.num_kt; ++kt, ++step) {
+        for (int kt = sg.kt0; kt < kte; ++kt, ++step) {
           // the operand tiles landed (a pair's full barrier counts both CTAs' bytes) and
           // the stage's scales are in TMEM
           if (!mbar_wait_bounded(full_bar(s), ph, abort_flag, prm.status, kStatusTimeoutMma, tmo) ||
@@ -545,7 +606,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           const uint32_t sfq_col = sfp_col + C_::kSfpCols + sfq_shift;
           const uint64_t pdesc = make_smem_desc(base + stage_off(s), 0, C_::kSbo, C_::kSwizzle);
           const uint64_t qdesc = make_smem_desc(base + stage_off(s) + kOffQ, 0, C_::kSbo, C_::kSwizzle);
-          const uint32_t acc0 = kt > 0 ? 1u : 0u;
+          const uint32_t acc0 = kt > sg.kt0 ? 1u : 0u;
           if (prm.debug & 4) {
           } else if (k_blocks(ti, kt) == KB) {
 #pragma unroll
@@ -627,11 +688,14 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     // their slot, write them, and arrive on the stage's sf_full (the leader's, for a pair).
     int sl = 0;
     uint32_t slph = 0;
-    for (int t = work0; t < total && ok; t += work_step) {
+    Seg sg;
+    for (bool more = seg_first(prm, total, work0, work_step, sg); more && ok;
+         more = seg_next(prm, total, work0, work_step, sg)) {
       TileInfo ti;
-      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, t, ti);
+      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg.t, ti);
       const int nq_atoms = q_atoms(ti);
-      for (int kt = 0; kt < ti.num_kt && ok; ++kt, ++tstep) {
+      const int kte = min(sg.kt1, ti.num_kt);
+      for (int kt = sg.kt0; kt < kte && ok; ++kt, ++tstep) {
         const int cs = s;
         const uint32_t cph = ph;
         if (++s == S) { s = 0; ph ^= 1; }
@@ -679,15 +743,87 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     const int quad = warp & 3;
     const int half = warp >> 2;
     const int row = quad * 32 + lane;  // TMEM lane == accumulator row
-    for (int t = work0; t < total; t += work_step) {
+    Seg sg;
+    for (bool more = seg_first(prm, total, work0, work_step, sg); more;
+         more = seg_next(prm, total, work0, work_step, sg)) {
       TileInfo ti;
-      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, t, ti);
+      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg.t, ti);
       if (!mbar_wait_bounded(accf_bar(acc), aph, abort_flag, prm.status, kStatusTimeoutEpilogue,
                              tmo)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + half * kHalf;
       const int q_lo = ti.q0 + half * kHalf;
       uint32_t pk[kChunks][16];
+      if constexpr (!GROUPED && !CTA2 && BN <= 128) {
+        if (prm.sk_ktn && (sg.kt0 > 0 || sg.kt1 < ti.num_kt)) {
+          // ---- stream-K piece of a split tile: fp32 partials meet in the owner CTA, the
+          // one holding k-step 0 (its last segment); the others (each CTA's first segment)
+          // publish theirs in their slot: column group g, row r at float4 index g * 128 + r.
+          float a[kHalf];
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              uint32_t r[16];
+              tmem_ld_32x32b_x16(t_row + c * 32 + hh * 16, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) a[c * 32 + hh * 16 + j] = __uint_as_float(r[j]);
+            }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) arrive_leader(acce_bar(acc));
+          if (++acc == A) { acc = 0; aph ^= 1; }
+          const int cg0 = half * kHalf / 4;  // this warp's first column group
+          float4* mine = reinterpret_cast<float4*>(prm.sk_slots) + (size_t)blockIdx.x * (BN / 4) * 128;
+          if (sg.kt0 > 0) {
+#pragma unroll
+            for (int g = 0; g < kHalf / 4; ++g)
+              __stcg(mine + (cg0 + g) * 128 + row,
+                     make_float4(a[4 * g], a[4 * g + 1], a[4 * g + 2], a[4 * g + 3]));
+            named_barrier_sync(1, 32 * kEpiWarps);
+            if (threadIdx.x == 0) st_release_gpu(prm.sk_flags + blockIdx.x, kSkPublished);
+            continue;
+          }
+          // later CTAs holding pieces of this tile: c in [blockIdx.x + 1, c_end)
+          const int tile_end = (sg.t + 1) * prm.sk_ktn;
+          int c_end = blockIdx.x + 1;
+          while (c_end < (int)gridDim.x && sk_start(prm, c_end, work_step) < tile_end) ++c_end;
+          if (threadIdx.x == 0) {  // wait for every piece first: one L2 round trip for all
+            const uint64_t t0 = global_timer_ns();
+            for (int c = blockIdx.x + 1; c < c_end; ++c) {
+              while (ld_acquire_gpu(prm.sk_flags + c) != kSkPublished) {
+                if (*abort_flag || global_timer_ns() - t0 > tmo) {
+                  *abort_flag = 1;
+                  atomicCAS(prm.status, 0, kStatusTimeoutEpilogue);
+                  break;
+                }
+              }
+              prm.sk_flags[c] = 0u;
+            }
+          }
+          named_barrier_sync(1, 32 * kEpiWarps);
+          for (int c = blockIdx.x + 1; c < c_end; ++c) {
+            const float4* theirs =
+                reinterpret_cast<const float4*>(prm.sk_slots) + (size_t)c * (BN / 4) * 128;
+            float4 v[kHalf / 4];
+#pragma unroll
+            for (int g = 0; g < kHalf / 4; ++g) v[g] = __ldcg(theirs + (cg0 + g) * 128 + row);
+#pragma unroll
+            for (int g = 0; g < kHalf / 4; ++g) {
+              a[4 * g] += v[g].x; a[4 * g + 1] += v[g].y; a[4 * g + 2] += v[g].z; a[4 * g + 3] += v[g].w;
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c)
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              __half2 h = __floats2half2_rn(a[c * 32 + 2 * j], a[c * 32 + 2 * j + 1]);
+              pk[c][j] = *reinterpret_cast<uint32_t*>(&h);
+            }
+          goto store_tile;
+        }
+      }
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
         if (q_lo + c * 32 < ti.q_rows && !(prm.debug & 64)) {  // warp-uniform
@@ -707,11 +843,12 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       tc_fence_before();
       __syncwarp();
       if (lane == 0) arrive_leader(acce_bar(acc));
+      if (++acc == A) { acc = 0; aph ^= 1; }
+    store_tile:
       if (threadIdx.x == 0) {
         if (etile == 0) trace_cta(prm, 2);
         trace_event(tsm, 5, etile++ - tbase / 32u);
       }
-      if (++acc == A) { acc = 0; aph ^= 1; }
       const int p = ti.p0 + row;
       if (p < ti.p_rows && !(prm.debug & 16)) {
 #pragma unroll

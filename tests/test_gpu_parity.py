@@ -73,6 +73,31 @@ def test_tile_configs_ragged(cuda, cfg, m, n, k, l):
     assert_close(got, dense_expected(data), f"order={order} bn={bn} {m}x{n}x{k}x{l}")
 
 
+# stream-K (fp32 partials of split tiles reduced by the CTA holding k-step 0): forced on and
+# off, down to one tile over many CTAs, ragged edges, a partial last k-stage, batches
+SK_SHAPES = [(64, 128, 2048, 1), (100, 300, 1088, 1), (128, 4096, 7168, 1), (64, 14336, 4096, 1),
+             (200, 100, 1280, 2), (1, 64, 4096, 1)]
+
+
+@pytest.mark.parametrize("bn", [64, 128])
+@pytest.mark.parametrize("sk", [1, 2])
+@pytest.mark.parametrize("m,n,k,l", SK_SHAPES)
+def test_stream_k(cuda, bn, sk, m, n, k, l):
+    data = inputs.generate_input(m, n, k, l, seed=11)
+    got = _run_dense(data, opt=_native.options(operand_order=2, tile_n=bn, stream_k=sk))
+    assert_close(got, dense_expected(data), f"stream_k={sk} bn={bn} {m}x{n}x{k}x{l}")
+
+
+def test_stream_k_max_ctas_and_repeat(cuda):
+    data = inputs.generate_input(128, 512, 4096, 1, seed=13)
+    exp = dense_expected(data)
+    for ctas in (5, 37, 148):
+        opt = _native.options(operand_order=2, tile_n=128, stream_k=2, max_ctas=ctas)
+        first = _run_dense(data, opt=opt).copy()
+        assert_close(first, exp, f"max_ctas={ctas}")
+        assert np.array_equal(first.view(np.uint16), _run_dense(data, opt=opt).view(np.uint16))
+
+
 def test_guard_bands_untouched(cuda):
     m, n, k = 200, 264, 512
     data = list(inputs.generate_input(m, n, k, 1, seed=3))

@@ -61,9 +61,14 @@ typedef struct nvfp4_options {
                                      followed by 4 stamps per CTA (entry, start, first tile, exit) */
   int stage_k;                    /* 0 = auto; 128 or 256 K elements per pipeline stage */
   int cta_pair;                   /* 0 = auto, 1 = off, 2 = M=256 tiles on a CTA pair (cta_group::2) */
-  int stream_k;                   /* dense: 0 = auto (when tiles < SMs), 1 = off, 2 = on.  Stream-K
+  int stream_k;                   /* dense: 0 / 1 = off, 2 = on (k-steps split evenly over all SMs).  Stream-K
                                      keeps a small per-stream workspace (flags + fp32 partials,
                                      ~16 MiB) allocated on first use outside stream capture */
+  /* Fused epilogue, dense GEMM only (the grouped entry points reject it):
+   *   C[m, n] = act(acc[m, n] + bias[n]), rounded to the output type. */
+  const float* bias;              /* NULL, or N fp32 values (device), the same for every batch */
+  int activation;                 /* 0 = none, 1 = relu, 2 = gelu (erf form) */
+  int out_dtype;                  /* 0 = fp16, 1 = bf16 (c holds bf16) */
 } nvfp4_options;
 
 /* Human-readable message for the last error returned on this thread. */

@@ -59,6 +59,9 @@ class Nvfp4Options(ctypes.Structure):
         ("stage_k", ctypes.c_int),
         ("cta_pair", ctypes.c_int),
         ("stream_k", ctypes.c_int),
+        ("bias", ctypes.c_void_p),
+        ("activation", ctypes.c_int),
+        ("out_dtype", ctypes.c_int),
     ]
 
 
@@ -139,6 +142,6 @@ def raise_on_device_error() -> None:
 
 
 def options(operand_order=0, tile_n=0, max_ctas=0, timeout_ns=0, debug=0, trace=None, stage_k=0,
-            cta_pair=0, stream_k=0):
+            cta_pair=0, stream_k=0, bias=None, activation=0, out_dtype=0):
     return Nvfp4Options(operand_order, tile_n, max_ctas, timeout_ns, debug, trace, stage_k, cta_pair,
-                        stream_k)
+                        stream_k, bias, activation, out_dtype)

@@ -209,12 +209,12 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   return e;
 }
 
-template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false>
+template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false, bool SK = false>
 int launch(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tsp,
            const CUtensorMap& tsq, const GemmParams& prm, int grid,
            cudaStream_t stream) {
   using C_ = Cfg<BN, KB, CTA2>;
-  auto kern = nvfp4_gemm_kernel<GROUPED, SWAP, BN, KB, CTA2>;
+  auto kern = nvfp4_gemm_kernel<GROUPED, SWAP, BN, KB, CTA2, SK>;
   static bool attr_done[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -230,7 +230,7 @@ int launch(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tsp,
     attr_done[dev] = true;
   }
   cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kNumThreads), smem, stream,
-                             CTA2 ? 2 : 1, prm.sk_ktn > 0, tp, tq, tsp, tsq, prm);
+                             CTA2 ? 2 : 1, SK, tp, tq, tsp, tsq, prm);
   if (e != cudaSuccess) return cuda_fail(e, "nvfp4_gemm_kernel launch");
   return NVFP4_OK;
 }
@@ -355,6 +355,11 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   prm.timeout_ns = (opt && opt->timeout_ns) ? opt->timeout_ns : g_timeout_ns;
   prm.debug = opt ? opt->debug : 0;
   prm.trace = opt ? reinterpret_cast<unsigned long long*>(opt->trace) : nullptr;
+  if (opt) {
+    prm.bias = opt->bias;
+    prm.act = opt->activation;
+    prm.out_bf16 = opt->out_dtype == 1;
+  }
   int grid = st->num_sms;
   if (opt && opt->max_ctas > 0 && opt->max_ctas < grid) grid = opt->max_ctas;
   if (CTA2) {
@@ -365,20 +370,18 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   } else if (grid > prm.total_tiles) {
     grid = prm.total_tiles;
   }
-  // Stream-K when the tiles would leave most SMs idle (skinny M, few tiles, long K): every
-  // CTA takes an equal share of all k-steps, and a split tile's fp32 partials meet in the
-  // CTA holding its k-step 0.  The reduction costs about one L2 round trip per piece, so
-  // auto mode needs tiles <= SMs / 2 and >= 16 k-steps per tile, and splits a tile into
-  // 2 pieces (>= 48 k-steps) or 3 (B200, M = 128: 128 x 7168 x 16384 36 -> 27 us,
-  // 128 x 1536 x 7168 17.7 -> 15.3 us; shorter K or more pieces lose).  stream_k = 2 uses
-  // every SM (or max_ctas).  BN <= 128 (the fp32 partial fits in registers); no CTA pairs.
+  // Stream-K (option stream_k = 2; off by default): every CTA takes an equal share of all
+  // k-steps and a split tile's fp32 partials meet in the CTA holding its k-step 0.  Measured
+  // on B200 against the plain schedule it does not pay for these skinny shapes (M = 128:
+  // 128 x 4096 x 7168 20.5 vs 15.3 us, 128 x 1536 x 7168 18.7 vs 14.8 us, 128 x 7168 x 16384
+  // 30.2 vs 30.4 us; c1 15.6 vs 12.2 us): the HBM stream of the tiles' CTAs is already close
+  // to what more SMs get, and the reduction adds an L2 round trip.  BN <= 128, no CTA pairs.
   const int ktn = (k + KB * 64 - 1) / (KB * 64);
   const int sk_opt = opt ? opt->stream_k : 0;
-  const bool sk_auto = sk_opt == 0 && 2 * prm.total_tiles <= st->num_sms && ktn >= 16;
-  if (!CTA2 && BN <= 128 && ktn >= 2 && (sk_opt == 2 || sk_auto)) {
+  const bool sk_auto = false;
+  if constexpr (!CTA2 && BN <= 128) if (ktn >= 2 && (sk_opt == 2 || sk_auto)) {
     int g = st->num_sms;
     if (opt && opt->max_ctas > 0 && opt->max_ctas < g) g = opt->max_ctas;
-    if (sk_auto) g = std::min(g, (ktn >= 48 ? 2 : 3) * prm.total_tiles);
     if ((long long)prm.total_tiles * ktn < g) g = prm.total_tiles * ktn;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -389,7 +392,7 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
       prm.sk_ktn = ktn;
       prm.sk_flags = static_cast<unsigned*>(ws);
       prm.sk_slots = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kSkMaxCtas * sizeof(unsigned));
-      rc = launch<false, SWAP, BN, KB, CTA2>(tp, tq, tsp, tsq, prm, g, stream);
+      rc = launch<false, SWAP, BN, KB, CTA2, true>(tp, tq, tsp, tsq, prm, g, stream);
       if (rc == NVFP4_OK) return rc;
       // (a cooperative launch the device refuses: run the plain schedule instead)
       cudaGetLastError();
@@ -587,6 +590,10 @@ int nvfp4_gemm_ex(const void* a, const void* b, const void* sfa_perm, const void
     return fail(NVFP4_ERR_ALIGNMENT, "a, b and the scale tensors must be 16-byte aligned");
   if ((reinterpret_cast<uintptr_t>(c) & 1u) != 0)
     return fail(NVFP4_ERR_ALIGNMENT, "c must be 2-byte aligned");
+  if (opt && (opt->activation < 0 || opt->activation > 2 || opt->out_dtype < 0 || opt->out_dtype > 1))
+    return fail(NVFP4_ERR_INVALID_ARG, "activation must be 0..2 and out_dtype 0..1");
+  if (opt && opt->bias && (reinterpret_cast<uintptr_t>(opt->bias) & 3u) != 0)
+    return fail(NVFP4_ERR_ALIGNMENT, "bias must be 4-byte aligned");
   DeviceState* st = nullptr;
   int rc = device_state(&st);
   if (rc) return rc;
@@ -632,6 +639,8 @@ size_t nvfp4_grouped_gemm_workspace_size(int G) {
 int nvfp4_grouped_gemm_ex(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev,
                           const uint64_t* sf_ptrs_dev, int G, void* workspace,
                           size_t workspace_bytes, void* stream, const nvfp4_options* opt) {
+  if (opt && (opt->bias || opt->activation || opt->out_dtype))
+    return fail(NVFP4_ERR_UNSUPPORTED, "the fused epilogue (bias, activation, out_dtype) is dense-only");
   if (G <= 0 || G > kMaxGroups)
     return fail(NVFP4_ERR_UNSUPPORTED, "group count %d outside [1, %d]", G, kMaxGroups);
   if (!sizes_dev || !abc_ptrs_dev || !sf_ptrs_dev)

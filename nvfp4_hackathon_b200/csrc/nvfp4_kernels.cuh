@@ -41,6 +41,7 @@
 // all four quarters.
 #pragma once
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
 #include "ptx_sm100.cuh"
@@ -143,6 +144,10 @@ struct GemmParams {
   int sk_ktn;
   float* sk_slots;              // per CTA: BN/4 x 128 float4 (column group major)
   unsigned* sk_flags;           // per CTA: kSkPublished while its partial is published
+  // fused epilogue (dense): out = act(acc + bias[n]) stored as fp16 or bf16
+  const float* bias;            // per output column n, or null
+  int act;                      // 0 none, 1 relu, 2 gelu (erf form)
+  int out_bf16;                 // 1: C is bf16
   // control
   int* status;
   unsigned long long timeout_ns;
@@ -209,8 +214,9 @@ struct Seg {
 __device__ __forceinline__ int sk_start(const GemmParams& prm, int w, int nwork) {
   return (int)((long long)prm.total_tiles * prm.sk_ktn * w / nwork);
 }
+template <bool SK>
 __device__ __forceinline__ bool seg_first(const GemmParams& prm, int total, int w, int step, Seg& sg) {
-  if (prm.sk_ktn) {
+  if constexpr (SK) {
     const int b = sk_start(prm, w, step), e = sk_start(prm, w + 1, step);
     if (b >= e) return false;
     sg.t = b / prm.sk_ktn;
@@ -223,8 +229,9 @@ __device__ __forceinline__ bool seg_first(const GemmParams& prm, int total, int 
   sg.kt1 = 0x7fffffff;
   return w < total;
 }
+template <bool SK>
 __device__ __forceinline__ bool seg_next(const GemmParams& prm, int total, int w, int step, Seg& sg) {
-  if (prm.sk_ktn) {
+  if constexpr (SK) {
     const int e = sk_start(prm, w + 1, step);
     sg.t += 1;
     if (sg.t * prm.sk_ktn >= e) return false;
@@ -296,12 +303,31 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtenso
   }
 }
 
-template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false>
+// Fused epilogue: bias of output column n, activation, then the output type's rounding.
+__device__ __forceinline__ float epi_post(const GemmParams& prm, float v, int n, int ncols) {
+  if (prm.bias && n < ncols) v += __ldg(prm.bias + n);
+  if (prm.act == 1) v = fmaxf(v, 0.f);
+  else if (prm.act == 2) v = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+  return v;
+}
+__device__ __forceinline__ uint32_t epi_pack(const GemmParams& prm, float x, float y) {
+  if (prm.out_bf16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __half2 h = __floats2half2_rn(x, y);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// SK: stream-K schedule (dense, BN <= 128); a separate instantiation so that the plain
+// schedule's code is not touched by it.
+template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false, bool SK = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
 nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constant__ CUtensorMap tm_q,
                   const __grid_constant__ CUtensorMap tm_sfp, const __grid_constant__ CUtensorMap tm_sfq,
                   const GemmParams prm) {
   static_assert(!(CTA2 && GROUPED), "CTA pairs are used for the dense GEMM only");
+  static_assert(!SK || (!GROUPED && !CTA2 && BN <= 128), "stream-K: dense, 1-CTA, BN <= 128");
   using C_ = Cfg<BN, KB, CTA2>;
   constexpr int S = C_::kStages;
   constexpr int A = C_::kAccStages;
@@ -379,7 +405,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     // (L2 is the point of coherence, nothing lands in this SM).  Dense only: the grouped
     // schedule is itself written by the preceding prep kernel.
     Seg sg0;
-    if (seg_first(prm, prm.total_tiles, work0, work_step, sg0)) {
+    if (seg_first<SK>(prm, prm.total_tiles, work0, work_step, sg0)) {
       TileInfo ti;
       decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg0.t, ti);
       const int kte = min(sg0.kt1, ti.num_kt);
@@ -412,7 +438,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   if (threadIdx.x == 0) trace_cta(prm, 1);
   // stream-K: this CTA's partial is not published yet (the owner of a tile also clears the
   // flags it consumed; this covers a launch that ended early)
-  if (!GROUPED && prm.sk_ktn && threadIdx.x == 0) prm.sk_flags[blockIdx.x] = 0u;
+  if (SK && threadIdx.x == 0) prm.sk_flags[blockIdx.x] = 0u;
 
   const int total = GROUPED ? __ldg(prm.tile_prefix + prm.G) : prm.total_tiles;
   const uint64_t tmo = prm.timeout_ns;
@@ -458,12 +484,12 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       };
       auto cur_next = [&](Cursor& c) {
         if (++c.kt == c.kte) {
-          c.valid = seg_next(prm, total, work0, work_step, c.sg);
+          c.valid = seg_next<SK>(prm, total, work0, work_step, c.sg);
           cur_load(c);
         }
       };
       Cursor sfc;
-      sfc.valid = seg_first(prm, total, work0, work_step, sfc.sg);
+      sfc.valid = seg_first<SK>(prm, total, work0, work_step, sfc.sg);
       cur_load(sfc);
       int sl = 0;
       uint32_t slph = 0;
@@ -507,8 +533,8 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       // scale atoms of steps 0 .. LEAD-1 go out first (their slots are fresh)
       for (int j = 0; j < LEAD; ++j) sf_step(j % kNumProducers == (int)pid);
       Seg sg;
-      for (bool more = seg_first(prm, total, work0, work_step, sg); more && ok;
-           more = seg_next(prm, total, work0, work_step, sg)) {
+      for (bool more = seg_first<SK>(prm, total, work0, work_step, sg); more && ok;
+           more = seg_next<SK>(prm, total, work0, work_step, sg)) {
         TileInfo ti;
         decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg.t, ti);
         if (GROUPED && ti.map_p != last_map) {
@@ -572,8 +598,8 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       uint32_t ph = 0;
       uint32_t step = 0;
       Seg sg;
-      for (bool more = seg_first(prm, total, work0, work_step, sg); more && ok;
-           more = seg_next(prm, total, work0, work_step, sg)) {
+      for (bool more = seg_first<SK>(prm, total, work0, work_step, sg); more && ok;
+           more = seg_next<SK>(prm, total, work0, work_step, sg)) {
         TileInfo ti;
         decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg.t, ti);
         const int kte = min(sg.kt1, ti.num_kt);
@@ -689,8 +715,8 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     int sl = 0;
     uint32_t slph = 0;
     Seg sg;
-    for (bool more = seg_first(prm, total, work0, work_step, sg); more && ok;
-         more = seg_next(prm, total, work0, work_step, sg)) {
+    for (bool more = seg_first<SK>(prm, total, work0, work_step, sg); more && ok;
+         more = seg_next<SK>(prm, total, work0, work_step, sg)) {
       TileInfo ti;
       decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg.t, ti);
       const int nq_atoms = q_atoms(ti);
@@ -744,8 +770,8 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     const int half = warp >> 2;
     const int row = quad * 32 + lane;  // TMEM lane == accumulator row
     Seg sg;
-    for (bool more = seg_first(prm, total, work0, work_step, sg); more;
-         more = seg_next(prm, total, work0, work_step, sg)) {
+    for (bool more = seg_first<SK>(prm, total, work0, work_step, sg); more;
+         more = seg_next<SK>(prm, total, work0, work_step, sg)) {
       TileInfo ti;
       decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg.t, ti);
       if (!mbar_wait_bounded(accf_bar(acc), aph, abort_flag, prm.status, kStatusTimeoutEpilogue,
@@ -753,9 +779,11 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + half * kHalf;
       const int q_lo = ti.q0 + half * kHalf;
+      const bool fused = prm.bias || prm.act || prm.out_bf16;  // (warp-uniform)
+      const int ncols = SWAP ? ti.p_rows : ti.q_rows;          // output columns N
       uint32_t pk[kChunks][16];
-      if constexpr (!GROUPED && !CTA2 && BN <= 128) {
-        if (prm.sk_ktn && (sg.kt0 > 0 || sg.kt1 < ti.num_kt)) {
+      if constexpr (SK) {
+        if (sg.kt0 > 0 || sg.kt1 < ti.num_kt) {
           // ---- stream-K piece of a split tile: fp32 partials meet in the owner CTA, the
           // one holding k-step 0 (its last segment); the others (each CTA's first segment)
           // publish theirs in their slot: column group g, row r at float4 index g * 128 + r.
@@ -806,20 +834,27 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           for (int c = blockIdx.x + 1; c < c_end; ++c) {
             const float4* theirs =
                 reinterpret_cast<const float4*>(prm.sk_slots) + (size_t)c * (BN / 4) * 128;
-            float4 v[kHalf / 4];
+            constexpr int kRound = 8;  // float4 loads in flight per thread (register budget)
 #pragma unroll
-            for (int g = 0; g < kHalf / 4; ++g) v[g] = __ldcg(theirs + (cg0 + g) * 128 + row);
+            for (int g0 = 0; g0 < kHalf / 4; g0 += kRound) {
+              float4 v[kRound];
 #pragma unroll
-            for (int g = 0; g < kHalf / 4; ++g) {
-              a[4 * g] += v[g].x; a[4 * g + 1] += v[g].y; a[4 * g + 2] += v[g].z; a[4 * g + 3] += v[g].w;
+              for (int g = 0; g < kRound; ++g) v[g] = __ldcg(theirs + (cg0 + g0 + g) * 128 + row);
+#pragma unroll
+              for (int g = 0; g < kRound; ++g) {
+                float* d = a + 4 * (g0 + g);
+                d[0] += v[g].x; d[1] += v[g].y; d[2] += v[g].z; d[3] += v[g].w;
+              }
             }
           }
 #pragma unroll
           for (int c = 0; c < kChunks; ++c)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              __half2 h = __floats2half2_rn(a[c * 32 + 2 * j], a[c * 32 + 2 * j + 1]);
-              pk[c][j] = *reinterpret_cast<uint32_t*>(&h);
+              const int n0 = SWAP ? ti.p0 + row : q_lo + c * 32 + 2 * j;
+              const int n1 = SWAP ? n0 : n0 + 1;
+              pk[c][j] = epi_pack(prm, epi_post(prm, a[c * 32 + 2 * j], n0, ncols),
+                                  epi_post(prm, a[c * 32 + 2 * j + 1], n1, ncols));
             }
           goto store_tile;
         }
@@ -832,10 +867,20 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
             uint32_t r[16];
             tmem_ld_32x32b_x16(t_row + c * 32 + hh * 16, r);
             tmem_ld_wait();
+            if (!fused) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              __half2 h = __floats2half2_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-              pk[c][hh * 8 + j] = *reinterpret_cast<uint32_t*>(&h);
+              for (int j = 0; j < 8; ++j) {
+                __half2 h = __floats2half2_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+                pk[c][hh * 8 + j] = *reinterpret_cast<uint32_t*>(&h);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int n0 = SWAP ? ti.p0 + row : q_lo + c * 32 + hh * 16 + 2 * j;
+                const int n1 = SWAP ? n0 : n0 + 1;
+                pk[c][hh * 8 + j] = epi_pack(prm, epi_post(prm, __uint_as_float(r[2 * j]), n0, ncols),
+                                             epi_post(prm, __uint_as_float(r[2 * j + 1]), n1, ncols));
+              }
             }
           }
         }

@@ -115,7 +115,7 @@ int nvfp4_grouped_gemm(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev,
                        const uint64_t* sf_ptrs_dev, int G, void* workspace, size_t workspace_bytes,
                        void* stream);
 
-/* Same with tuning / test options (tile_n = 64, 128 or 256 token rows per tile). */
+/* Same with tuning / test options (tile_n = 64, 128, 192 or 256 token rows per tile). */
 int nvfp4_grouped_gemm_ex(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev,
                           const uint64_t* sf_ptrs_dev, int G, void* workspace,
                           size_t workspace_bytes, void* stream, const nvfp4_options* opt);

@@ -660,6 +660,7 @@ int nvfp4_grouped_gemm_ex(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev
       if (opt && opt->stage_k == 128)
         return run_grouped_bn<128, 2>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
       return run_grouped_bn<128>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
+    case 192: return run_grouped_bn<192>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
     case 256: return run_grouped_bn<256>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
     default: return fail(NVFP4_ERR_UNSUPPORTED, "grouped tile_n %d not built", bn);
   }

@@ -68,7 +68,7 @@ constexpr int kSmemBudget = kMaxDynamicSmem - 2560;  // minus alignment, barrier
 // shared memory, so stages are released and refilled at half the granularity.
 template <int BN, int KB, bool CTA2 = false>
 struct Cfg {
-  static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
+  static_assert(BN == 64 || BN == 128 || BN == 192 || BN == 256, "BN must be 64, 128, 192 or 256");
   static_assert(KB == 2 || KB == 4, "KB must be 2 or 4");
   static constexpr int kBKBytes = KB * 32;            // bytes of K per stage per row
   static constexpr int kBK = KB * 64;                 // K elements per stage

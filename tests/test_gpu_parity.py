@@ -163,7 +163,7 @@ REF_GROUP_CASES = [
 ]
 
 
-@pytest.mark.parametrize("bn,stage_k", [(64, 0), (128, 0), (256, 0), (128, 128)])
+@pytest.mark.parametrize("bn,stage_k", [(64, 0), (128, 0), (192, 0), (256, 0), (128, 128)])
 @pytest.mark.parametrize("case", range(len(REF_GROUP_CASES)))
 def test_reference_group_cases(cuda, case, bn, stage_k):
     m, n, k = REF_GROUP_CASES[case]

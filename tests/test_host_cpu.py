@@ -74,3 +74,12 @@ def _gather_worker(rank, world, port, n, m):
 
 def test_column_gather_two_ranks_gloo():
     mp.spawn(_gather_worker, args=(2, _free_port(), 1000, 3), nprocs=2, join=True)
+
+
+def test_grouped_tile_choice():
+    from nvfp4_hackathon_b200 import group_gemm
+    c3 = [(m, 4096, 7168, 1) for m in inputs.uniform_group_sizes(8, 1111)]
+    c4a = [(m, 2048, 7168, 1) for m in inputs.zipf_group_sizes(64, 32768)]
+    assert group_gemm.choose_tile_n(c3, 148) == 192
+    assert group_gemm.choose_tile_n(c4a, 148) == 256
+    assert group_gemm.choose_tile_n([(0, 4096, 7168, 1)], 148) in (128, 192, 256)

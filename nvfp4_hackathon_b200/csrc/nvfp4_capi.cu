@@ -686,7 +686,8 @@ int nvfp4_quantize(const void* x, int dtype, int rows, int k, int l, void* codes
   DeviceState* st = nullptr;
   int rc = device_state(&st);
   if (rc) return rc;
-  const dim3 grid((k / 64 + kQuantAtoms - 1) / kQuantAtoms, rm, l);
+  const int atoms = dtype == kQuantF32 ? quant_atoms<kQuantF32>() : quant_atoms<kQuantF16>();
+  const dim3 grid((k / 64 + atoms - 1) / atoms, rm, l);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto* c8 = static_cast<uint8_t*>(codes);
   auto* sp = static_cast<uint8_t*>(sf_perm);

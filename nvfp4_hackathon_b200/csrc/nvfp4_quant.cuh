@@ -16,12 +16,12 @@
 // 64-wide K block one 512-byte atom; row r, K-vector j at byte (r % 32) * 16 + (r / 32) * 4 + j.
 // Rows past `rows` in the last block get scale 0, like the reference's padding.
 //
-// HBM-bound.  A CTA of 8 warps covers 128 rows x 4 atoms (256 elements of K); a warp
-// takes 16 rows, and per row reads 256 contiguous elements with one 16-byte load per lane
-// (two for fp32): lane l holds elements 8l .. 8l+7, half of 16-element block l/2, and
-// the pair of lanes of a block reduces its amax with one shuffle.  Every load covers a
-// whole 512-byte (1 KiB) stretch of one row, every code store 128 contiguous bytes; the
-// CTA's scales are assembled in shared memory and leave as 2 KiB of whole atoms.
+// HBM-bound.  A CTA of 8 warps covers 128 rows x (32 lanes x 32 bytes) of input; a warp
+// takes 16 rows, and per row each lane reads 32 contiguous bytes: 16 elements (one block)
+// of fp16/bf16, or 8 fp32 elements (half a block; the pair of lanes reduces the block's amax
+// with one shuffle).  Every load instruction covers 512 contiguous bytes of one row, the
+// code stores are contiguous too, and the CTA's scales are assembled in shared memory and
+// leave as whole atoms (4 or 8 of them).
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -32,23 +32,27 @@ namespace nvfp4 {
 
 enum QuantDtype : int { kQuantF32 = 0, kQuantF16 = 1, kQuantBF16 = 2 };
 
+// 32 bytes of input (two 16-byte vectors already in registers) -> 8 or 16 floats: fp32
+// uses both vectors for 8 values; 16-bit types use one vector per 8 values.
 template <int DT>
-__device__ __forceinline__ void load8(const void* src, float (&v)[8]) {
+__device__ __forceinline__ void load8(const uint4* src, float (&v)[8]) {
   if constexpr (DT == kQuantF32) {
-    const float4* p = reinterpret_cast<const float4*>(src);
-    const float4 f0 = __ldg(p), f1 = __ldg(p + 1);
-    v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
-    v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+    const uint4 a = src[0], b = src[1];
+    v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y); v[2] = __uint_as_float(a.z); v[3] = __uint_as_float(a.w);
+    v[4] = __uint_as_float(b.x); v[5] = __uint_as_float(b.y); v[6] = __uint_as_float(b.z); v[7] = __uint_as_float(b.w);
   } else {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
+    const uint4 u = src[0];
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float2 f;
-      if constexpr (DT == kQuantF16) f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
-      else f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
-      v[2 * j] = f.x;
-      v[2 * j + 1] = f.y;
+      if constexpr (DT == kQuantF16) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+        v[2 * j] = f.x;
+        v[2 * j + 1] = f.y;
+      } else {  // bf16 is the upper half of an fp32: widening is exact
+        v[2 * j] = __uint_as_float(w[j] << 16);
+        v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+      }
     }
   }
 }
@@ -65,19 +69,32 @@ __device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
   return r;
 }
 
-constexpr int kQuantAtoms = 4;   // atoms (64 elements of K) per CTA
 constexpr int kQuantRowsPerWarp = 16;
 constexpr int kQuantBatch = 4;   // rows whose loads a warp keeps in flight together
+// Elements per lane: 32 bytes of input each, so fp32 lanes hold half a 16-element block
+// (pairs of lanes reduce the block's amax) and 16-bit lanes a whole block.
+template <int DT> __host__ __device__ constexpr int quant_epl() { return DT == kQuantF32 ? 8 : 16; }
+template <int DT> __host__ __device__ constexpr int quant_atoms() { return quant_epl<DT>() / 2; }  // atoms per CTA
 
 // Codes of 8 elements (half a block) given the block's scale; returns 4 packed bytes.
-// v = x / s is the correctly rounded division of the definition; negative values that
-// round to zero keep code 0 (the conversion would give -0).
+// The definition rounds the correctly rounded v = x / s.  q = x * (1 / s) is within ~1 ulp
+// of x / s, so both x / s and its rounding lie in [q (1 - 2^-21), q (1 + 2^-21)]; the
+// conversion is monotone, so where it agrees at both ends of that interval its result is
+// exact, and only a pair that straddles a rounding boundary pays for the division.
+// Negative values that round to zero keep code 0 (the conversion would give -0).
 __device__ __forceinline__ uint32_t e2m1_pack8(const float (&v)[8], float s) {
   uint32_t w = 0;
   if (s > 0.f) {
+    const float inv = 1.0f / s;
+    constexpr float kLo = 1.0f - 4.76837158203125e-07f, kHi = 1.0f + 4.76837158203125e-07f;  // 1 -+ 2^-21
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      w |= cvt_e2m1x2(__fdiv_rn(v[2 * i], s), __fdiv_rn(v[2 * i + 1], s)) << (8 * i);
+    for (int i = 0; i < 4; ++i) {
+      const float a = v[2 * i] * inv, b = v[2 * i + 1] * inv;
+      uint32_t c = cvt_e2m1x2(a * kLo, b * kLo);
+      if (c != cvt_e2m1x2(a * kHi, b * kHi))
+        c = cvt_e2m1x2(__fdiv_rn(v[2 * i], s), __fdiv_rn(v[2 * i + 1], s));
+      w |= c << (8 * i);
+    }
   }
   const uint32_t zero = ~(w | (w >> 1) | (w >> 2)) & 0x11111111u;  // magnitude-0 nibbles
   return w & ~(zero << 3);
@@ -85,52 +102,73 @@ __device__ __forceinline__ uint32_t e2m1_pack8(const float (&v)[8], float s) {
 
 // (4 CTAs of 8 warps per SM: other warps' loads cover a warp's compute phase)
 template <int DT>
-__global__ void __launch_bounds__(256, 4)
+__global__ void __launch_bounds__(256, DT == kQuantBF16 ? 3 : 4)
 nvfp4_quantize_kernel(const void* __restrict__ x, int rows, int k, uint8_t* __restrict__ codes,
                       uint8_t* __restrict__ sf_perm, uint8_t* __restrict__ sf_plain) {
-  __shared__ __align__(16) uint8_t atoms[kQuantAtoms * 512];
+  constexpr int EPL = quant_epl<DT>();
+  constexpr int ATOMS = quant_atoms<DT>();
+  __shared__ __align__(16) uint8_t atoms[ATOMS * 512];
   constexpr int kElem = DT == kQuantF32 ? 4 : 2;
   const int rk = k / 64;
   const int rm = (rows + 127) / 128;
-  const int kb0 = blockIdx.x * kQuantAtoms;  // first atom (64-wide K block) of this CTA
-  const int n_atoms = min(kQuantAtoms, rk - kb0);
+  const int kb0 = blockIdx.x * ATOMS;  // first atom (64-wide K block) of this CTA
+  const int n_atoms = min(ATOMS, rk - kb0);
   const int rb = blockIdx.y;
   const int l = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < kQuantAtoms * 512 / 16; i += blockDim.x)
+  for (int i = threadIdx.x; i < ATOMS * 512 / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(atoms)[i] = make_uint4(0, 0, 0, 0);
   __syncthreads();
-  const int blk = lane >> 1;              // 16-element block within the 256 elements
+  const int blk = lane * EPL / 16;        // 16-element block within the CTA's columns
   const int atom = blk >> 2, j = blk & 3;
   const bool lane_ok = atom < n_atoms;
-  const int col = kb0 * 64 + lane * 8;    // first element of this lane
+  const int col = kb0 * 64 + lane * EPL;  // first element of this lane
+  const bool writer = EPL == 16 || (lane & 1) == 0;
 #pragma unroll 1
   for (int r0 = 0; r0 < kQuantRowsPerWarp; r0 += kQuantBatch) {
-    float v[kQuantBatch][8];
+    // raw loads in flight (32 bytes per lane and row, whatever the type), converted later
+    uint4 raw[kQuantBatch][2];
 #pragma unroll
     for (int b = 0; b < kQuantBatch; ++b) {
       const int r = warp * kQuantRowsPerWarp + r0 + b;
       const int row = rb * 128 + r;
-      if (row < rows && lane_ok)
-        load8<DT>(static_cast<const uint8_t*>(x) + (((long long)l * rows + row) * k + col) * kElem, v[b]);
-      else
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[b][i] = 0.f;
+      const uint4* src = reinterpret_cast<const uint4*>(
+          static_cast<const uint8_t*>(x) + (((long long)l * rows + row) * k + col) * kElem);
+      if (row < rows && lane_ok) {
+        raw[b][0] = __ldg(src);
+        raw[b][1] = __ldg(src + 1);
+      } else {
+        raw[b][0] = raw[b][1] = make_uint4(0, 0, 0, 0);
+      }
     }
 #pragma unroll
     for (int b = 0; b < kQuantBatch; ++b) {
       const int r = warp * kQuantRowsPerWarp + r0 + b;
       const int row = rb * 128 + r;
+      float v[EPL];
+      load8<DT>(&raw[b][0], *reinterpret_cast<float(*)[8]>(&v[0]));
+      if constexpr (EPL == 16) load8<DT>(&raw[b][1], *reinterpret_cast<float(*)[8]>(&v[8]));
       float amax = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[b][i]));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      for (int i = 0; i < EPL; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      if constexpr (EPL == 8) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       if (row >= rows || !lane_ok) continue;
       const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(__fdiv_rn(amax, 6.0f), __NV_NOSAT, __NV_E4M3);
       const float s = float(*reinterpret_cast<const __nv_fp8_e4m3*>(&s8));
       const long long rowbase = (long long)l * rows + row;
-      *reinterpret_cast<uint32_t*>(codes + (rowbase * k + col) / 2) = e2m1_pack8(v[b], s);
-      if ((lane & 1) == 0) {
+      uint8_t* cdst = codes + (rowbase * k + col) / 2;
+      if constexpr (EPL == 16) {
+        float lo[8], hi[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { lo[i] = v[i]; hi[i] = v[8 + i]; }
+        *reinterpret_cast<uint2*>(cdst) = make_uint2(e2m1_pack8(lo, s), e2m1_pack8(hi, s));
+      } else {
+        float h[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) h[i] = v[i];
+        *reinterpret_cast<uint32_t*>(cdst) = e2m1_pack8(h, s);
+      }
+      if (writer) {
         atoms[atom * 512 + (r & 31) * 16 + (r >> 5) * 4 + j] = (uint8_t)s8;
         if (sf_plain) sf_plain[rowbase * (k / 16) + kb0 * 4 + blk] = (uint8_t)s8;
       }

@@ -17,8 +17,9 @@
 //               accumulator into registers as fp16, releases the accumulator, then stores
 //               to global while the next tile's MMAs already run
 //   warps 8-10  producers (k-steps round-robin): TMA loads of the P and Q tiles (128-byte
-//               swizzle) into a ring of kStages stages, and plain bulk copies of the scale
-//               atoms into their own ring of slots, kSfLead k-steps ahead of the operands
+//               swizzle) into a ring of kStages stages, and the scale atoms (dense: tensor
+//               loads through 8-byte-element scale maps; grouped: plain bulk copies) into
+//               their own ring of slots, kSfLead k-steps ahead of the operands
 //   warp 11     TMEM owner and MMA issuer: per k-step it waits for the stage's operand
 //               tiles (full) and scales (sf_full), issues tcgen05.mma kind::mxf4nvf4
 //               (K = 64 per instruction) and one tcgen05.commit to release the stage.

@@ -8,7 +8,8 @@ Default workload: configs[1] of BASELINE.json (M=64, N=14336, K=4096, L=1), one
 replica per GPU (the dense GEMM does not shard; scaling "weak").  Other
 workloads: c0, c2 (dense), c3 (grouped G=8), c4a (grouped G=64, experts sharded
 across ranks, strong scaling), c4b (dense 16384x28672x8192 sharded along N,
-strong scaling; ``--gather`` adds the NCCL all-gather of C).
+strong scaling; ``--gather`` gives every rank the whole C with an NCCL all-gather, or with
+``--gather p2p`` by the GEMM's own epilogue storing into every rank's C over NVLink).
 
 Prints one JSON line on rank 0.  ``value`` is the kernel throughput with inputs
 resident in HBM: the K steps rotate over enough input copies that they never hit
@@ -57,7 +58,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default="c1", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--gather", action="store_true", help="c4b: all-gather C shards (NCCL)")
+    ap.add_argument("--gather", nargs="?", const="nccl", default=None, choices=["nccl", "p2p"],
+                    help="c4b: every rank gets the whole C: nccl (default) = GEMM + NCCL all-gather; "
+                         "p2p = the GEMM's epilogue stores into every rank's C over NVLink")
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = min(steps, 50)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline budget")
     return ap.parse_args()
@@ -204,7 +207,19 @@ class Workload:
             self.global_flops = dense_flops(m, n, k)
             self.scaling = "strong"
             self.launches_per_step = 1
-            if gather and world > 1:
+            if gather == "p2p" and world > 1:
+                import torch.distributed as dist
+                # fused: the epilogue writes every rank's full C; a 1-element all-reduce
+                # orders the next reads after all ranks' kernels
+                self.c_full = torch.zeros((m, n), dtype=torch.float16, device=device)
+                self.peers = sharding.PeerBuffers(self.c_full, dist)
+                self.token = torch.zeros(1, dtype=torch.float32, device=device)
+
+                def run():
+                    sharding.gemm_allgather(self.data, self.peers, lo, n)
+                    dist.all_reduce(self.token)
+                self.run = run
+            elif gather and world > 1:
                 import torch.distributed as dist
                 lo0, hi0 = sharding.column_shard(n, world, 0)
                 gathered = torch.empty((world, m, hi0 - lo0), dtype=torch.float16, device=device)
@@ -414,7 +429,8 @@ def bench_ours(args):
                        "timing": ("K steps captured in one CUDA graph, replayed; CUDA events around the "
                                   "replays on the launching stream; max over ranks") if use_graph else
                                  "CUDA events around the K steps on the launching stream; max over ranks",
-                       "parallelism": f"{wl.scaling} x{world}"},
+                       "parallelism": f"{wl.scaling} x{world}",
+                       "gather": (args.gather or "none") if wl.kind == "dense_sharded" else "n/a"},
             "roofline": roof,
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,

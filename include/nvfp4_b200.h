@@ -121,6 +121,27 @@ int nvfp4_grouped_gemm_ex(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev
                           size_t workspace_bytes, void* stream, const nvfp4_options* opt);
 
 /*
+ * Dense GEMM writing C into several buffers at once (L = 1): outs[0 .. n_out), n_out <= 8,
+ * each already offset to this GEMM's first column, row stride ldc elements.  With the
+ * buffers of other GPUs (opened below) this is the N-sharded GEMM fused with the all-gather
+ * of C (configs[4] of the benchmark): every rank computes C[:, its columns] and its epilogue
+ * stores the tiles into every rank's full C over NVLink.  The reference has no multi-GPU
+ * path; the unfused form is its GEMM (kernels/gemm/submission.py:772-794) followed by an
+ * NCCL all-gather.  Callers order the peers' reads after this kernel (e.g. a barrier).
+ */
+int nvfp4_gemm_multi(const void* a, const void* b, const void* sfa_perm, const void* sfb_perm,
+                     const void* const* outs, int n_out, long long ldc, int m, int n, int k,
+                     void* stream);
+
+/* CUDA IPC for the buffers above: export a device pointer (handle of its allocation plus
+ * the pointer's offset in it), open a peer's handle (returns the allocation's base; add the
+ * offset), close it again.  nvfp4_ipc_handle_size() bytes per handle. */
+int nvfp4_ipc_handle_size(void);
+int nvfp4_ipc_get_handle(const void* dev_ptr, void* handle_out, unsigned long long* offset_out);
+int nvfp4_ipc_open_handle(const void* handle, void** dev_ptr_out);
+int nvfp4_ipc_close(void* dev_ptr);
+
+/*
  * Quantise x to NVFP4 on the GPU: the inputs the GEMMs take, computed from real values.
  * Replaces the host-side generation steps of the reference (kernels/gemm/reference.py:86-150:
  * per-16-element amax / 6 -> e4m3 scale, nearest e2m1 code, to_blocked scale permutation),

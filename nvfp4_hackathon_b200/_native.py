@@ -45,6 +45,11 @@ EXPORTED = (
     "nvfp4_grouped_gemm_ex",
     "nvfp4_grouped_gemm_noalloc",
     "nvfp4_quantize",
+    "nvfp4_gemm_multi",
+    "nvfp4_ipc_handle_size",
+    "nvfp4_ipc_get_handle",
+    "nvfp4_ipc_open_handle",
+    "nvfp4_ipc_close",
 )
 
 
@@ -111,6 +116,11 @@ def _load_slow() -> ctypes.CDLL:
                                               ctypes.POINTER(Nvfp4Options)]
         lib.nvfp4_grouped_gemm_noalloc.argtypes = [vp, vp, vp, i, vp]
         lib.nvfp4_quantize.argtypes = [vp, i, i, i, i, vp, vp, vp, vp]
+        lib.nvfp4_gemm_multi.argtypes = [vp, vp, vp, vp, vp, i, ctypes.c_longlong, i, i, i, vp]
+        lib.nvfp4_ipc_handle_size.argtypes = []
+        lib.nvfp4_ipc_get_handle.argtypes = [vp, vp, ctypes.POINTER(ull)]
+        lib.nvfp4_ipc_open_handle.argtypes = [vp, ctypes.POINTER(vp)]
+        lib.nvfp4_ipc_close.argtypes = [vp]
         for name in EXPORTED:
             getattr(lib, name)  # AttributeError here means a stale build
         _lib = lib

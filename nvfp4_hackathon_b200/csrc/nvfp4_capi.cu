@@ -309,6 +309,15 @@ void* sk_workspace(int dev, cudaStream_t stream) {
   return p;
 }
 
+// Several destinations for one dense GEMM's C (nvfp4_gemm_multi): set for the duration of
+// that call on this thread only.
+struct MultiOut {
+  int n;
+  long long ldc;
+  const void* ptr[8];
+};
+thread_local const MultiOut* g_multi_out = nullptr;
+
 template <bool SWAP, int BN, int KB, bool CTA2 = false>
 int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb, void* c, int m,
                  int n, int k, int l, cudaStream_t stream, DeviceState* st,
@@ -343,6 +352,12 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   prm.sf_q_batch = (long long)((q_rows + 127) / 128) * rk * kAtomBytes;
   prm.C = static_cast<__half*>(c);
   prm.ldc = n;
+  if (g_multi_out) {
+    prm.n_out = g_multi_out->n;
+    prm.ldc = g_multi_out->ldc;
+    for (int i = 0; i < g_multi_out->n; ++i)
+      prm.outs[i] = reinterpret_cast<unsigned long long>(g_multi_out->ptr[i]);
+  }
   prm.c_batch = (long long)m * n;
   const int pm = CTA2 ? 2 * kBM : kBM;  // P rows per tile (a CTA pair covers 256)
   prm.tiles_p = (p_rows + pm - 1) / pm;
@@ -624,6 +639,70 @@ int nvfp4_gemm_ex(const void* a, const void* b, const void* sfa_perm, const void
 #undef NVFP4_DENSE_CASE
   return fail(NVFP4_ERR_UNSUPPORTED, "no kernel for swap=%d tile_n=%d stage_k=%d", (int)ch.swap, ch.bn,
               ch.kb * 64);
+}
+
+int nvfp4_gemm_multi(const void* a, const void* b, const void* sfa_perm, const void* sfb_perm,
+                     const void* const* outs, int n_out, long long ldc, int m, int n, int k,
+                     void* stream) {
+  if (!outs || n_out < 1 || n_out > 8)
+    return fail(NVFP4_ERR_INVALID_ARG, "1..8 output buffers (got %d)", n_out);
+  if (ldc < n) return fail(NVFP4_ERR_INVALID_ARG, "ldc %lld < n %d", ldc, n);
+  MultiOut mo;
+  mo.n = n_out;
+  mo.ldc = ldc;
+  for (int i = 0; i < n_out; ++i) {
+    if (!outs[i] || (reinterpret_cast<uintptr_t>(outs[i]) & 1u))
+      return fail(NVFP4_ERR_ALIGNMENT, "output %d null or not 2-byte aligned", i);
+    mo.ptr[i] = outs[i];
+  }
+  g_multi_out = &mo;
+  const int rc = nvfp4_gemm_ex(a, b, sfa_perm, sfb_perm, const_cast<void*>(outs[0]), m, n, k, 1,
+                               stream, nullptr);
+  g_multi_out = nullptr;
+  return rc;
+}
+
+int nvfp4_ipc_handle_size(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+int nvfp4_ipc_get_handle(const void* dev_ptr, void* handle_out, unsigned long long* offset_out) {
+  if (!dev_ptr || !handle_out || !offset_out) return fail(NVFP4_ERR_INVALID_ARG, "null pointer");
+  // the handle names the whole allocation holding dev_ptr; its opener adds the offset back
+  using GetRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static GetRange get_range = nullptr;
+  if (!get_range) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return fail(NVFP4_ERR_DRIVER, "cuMemGetAddressRange not available");
+    get_range = reinterpret_cast<GetRange>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (get_range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+    return fail(NVFP4_ERR_DRIVER, "cuMemGetAddressRange failed");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = (unsigned long long)(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  return NVFP4_OK;
+}
+
+int nvfp4_ipc_open_handle(const void* handle, void** dev_ptr_out) {
+  // (returns the base of the exporter's allocation: add the exporter's offset)
+  if (!handle || !dev_ptr_out) return fail(NVFP4_ERR_INVALID_ARG, "null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  return NVFP4_OK;
+}
+
+int nvfp4_ipc_close(void* dev_ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return NVFP4_OK;
 }
 
 int nvfp4_gemm(const void* a, const void* b, const void* sfa_perm, const void* sfb_perm, void* c,

@@ -145,6 +145,10 @@ struct GemmParams {
   int sk_ktn;
   float* sk_slots;              // per CTA: BN/4 x 128 float4 (column group major)
   unsigned* sk_flags;           // per CTA: kSkPublished while its partial is published
+  // n_out > 0: store C into outs[0 .. n_out) instead (each already offset to this GEMM's
+  // columns, row stride ldc; peers' buffers reached over NVLink with plain stores), L = 1
+  int n_out;
+  unsigned long long outs[8];
   // fused epilogue (dense): out = act(acc + bias[n]) stored as fp16 or bf16
   const float* bias;            // per output column n, or null
   int act;                      // 0 none, 1 relu, 2 gelu (erf form)
@@ -896,13 +900,16 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         trace_event(tsm, 5, etile++ - tbase / 32u);
       }
       const int p = ti.p0 + row;
+      const int nout = prm.n_out > 0 ? prm.n_out : 1;
+      for (int d = 0; d < nout; ++d) {
+      __half* const Cd = prm.n_out > 0 ? reinterpret_cast<__half*>(prm.outs[d]) : ti.C;
       if (p < ti.p_rows && !(prm.debug & 16)) {
 #pragma unroll
         for (int c = 0; c < kChunks; ++c) {
           const int qc = q_lo + c * 32;
           if (qc >= ti.q_rows) break;
           if constexpr (!SWAP) {
-            __half* dst = ti.C + (long long)p * ti.ldc + qc;
+            __half* dst = Cd + (long long)p * ti.ldc + qc;
             if (qc + 32 <= ti.q_rows && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
               uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
@@ -917,7 +924,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
             }
           } else {
             // D[p=n, q=m] -> C[m, n]; lanes hold consecutive n, so each store is warp-coalesced
-            __half* dst = ti.C + (long long)qc * ti.ldc + p;
+            __half* dst = Cd + (long long)qc * ti.ldc + p;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               if (qc + j < ti.q_rows)
@@ -927,6 +934,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           }
         }
       }
+      }  // destinations
     }
     }
   }

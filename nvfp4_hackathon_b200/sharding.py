@@ -7,13 +7,17 @@
   piece) and assigns pieces longest-processing-time-first under a cost model of
   MMA time per token plus weight-load time per expert.
 * Dense GEMM (configs[4b]): each rank owns a contiguous block of N columns of B
-  and C; A is replicated.  ``gather_columns`` assembles the column shards on
-  every rank with one NCCL all-gather over NVLink when the caller wants them.
+  and C; A is replicated.  When every rank wants the whole C, ``gemm_allgather``
+  fuses the all-gather into the GEMM: each rank's epilogue stores its tiles into
+  every rank's full C (opened through CUDA IPC, ``PeerBuffers``) over NVLink, and
+  one tiny all-reduce orders the reads after all ranks' kernels.
+  ``gather_columns`` is the unfused alternative (one NCCL all-gather + re-interleave).
 
 The reference has no multi-GPU code; this module is the B200 build's own.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 # cost model (B200): fp4 MMA throughput and HBM bandwidth, used only for balancing
@@ -107,3 +111,62 @@ def assemble_columns(gathered, n: int, world: int):
         if hi > lo:
             parts.append(gathered[r, :, : hi - lo])
     return torch.cat(parts, dim=1)
+
+
+class PeerBuffers:
+    """Every rank's copy of one full-size buffer, usable from this process.
+
+    ``ptrs[r]`` is the device address of rank r's buffer (this rank's own tensor for r ==
+    rank, a CUDA IPC mapping of the peer's allocation otherwise).  Collective: every rank
+    constructs it with a tensor of the same shape, in the same order.
+    """
+
+    def __init__(self, tensor, dist):
+        from . import _native
+        self._lib = lib = _native.load()
+        rank, world = dist.get_rank(), dist.get_world_size()
+        hsize = lib.nvfp4_ipc_handle_size()
+        buf = ctypes.create_string_buffer(hsize)
+        off = ctypes.c_ulonglong()
+        _native.check(lib.nvfp4_ipc_get_handle(tensor.data_ptr(), buf, ctypes.byref(off)),
+                      "nvfp4_ipc_get_handle")
+        handles = [None] * world
+        dist.all_gather_object(handles, (buf.raw, off.value))
+        self.tensor = tensor
+        self.ptrs, self._opened = [], []
+        for r, (h, o) in enumerate(handles):
+            if r == rank:
+                self.ptrs.append(tensor.data_ptr())
+                continue
+            p = ctypes.c_void_p()
+            _native.check(lib.nvfp4_ipc_open_handle(ctypes.create_string_buffer(h, hsize), ctypes.byref(p)),
+                          "nvfp4_ipc_open_handle")
+            self._opened.append(p.value)
+            self.ptrs.append(p.value + o)
+
+    def close(self):
+        for p in self._opened:
+            self._lib.nvfp4_ipc_close(p)
+        self._opened = []
+
+
+def gemm_allgather(data, peers: PeerBuffers, col_lo: int, n_full: int, stream=None) -> None:
+    """C[:, col_lo : col_lo + n] of every rank's full (M, n_full) fp16 buffer = this rank's
+    A @ B_shard^T, in one kernel: the epilogue stores each tile to all ranks' buffers.
+
+    ``data`` is this rank's 7-tuple (L = 1; B holds the rank's n columns); its c is unused.
+    The peers may read their buffers only after every rank's kernel: follow with a
+    stream-ordered collective (``dist.all_reduce`` of a 1-element tensor) or a barrier.
+    """
+    import torch
+    from . import _native
+    a, b, _, _, sfa_p, sfb_p, _ = data
+    m, kb, l = a.shape
+    if l != 1:
+        raise ValueError("gemm_allgather needs L == 1")
+    n = b.shape[0]
+    outs = (ctypes.c_void_p * len(peers.ptrs))(*[p + 2 * col_lo for p in peers.ptrs])
+    s = torch.cuda.current_stream().cuda_stream if stream is None else stream
+    rc = peers._lib.nvfp4_gemm_multi(a.data_ptr(), b.data_ptr(), sfa_p.data_ptr(), sfb_p.data_ptr(),
+                                     outs, len(peers.ptrs), n_full, m, n, 2 * kb, s)
+    _native.check(rc, "nvfp4_gemm_multi")

@@ -900,9 +900,8 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         trace_event(tsm, 5, etile++ - tbase / 32u);
       }
       const int p = ti.p0 + row;
-      const int nout = prm.n_out > 0 ? prm.n_out : 1;
-      for (int d = 0; d < nout; ++d) {
-      __half* const Cd = prm.n_out > 0 ? reinterpret_cast<__half*>(prm.outs[d]) : ti.C;
+      // C itself, or (n_out > 0) every buffer of outs[]
+      auto store_c = [&](__half* const Cd) {
       if (p < ti.p_rows && !(prm.debug & 16)) {
 #pragma unroll
         for (int c = 0; c < kChunks; ++c) {
@@ -934,7 +933,14 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           }
         }
       }
-      }  // destinations
+      };
+      if (prm.n_out == 0) {
+        store_c(ti.C);
+      } else {
+#pragma unroll
+        for (int d = 0; d < 8; ++d)
+          if (d < prm.n_out) store_c(reinterpret_cast<__half*>(prm.outs[d]));
+      }
     }
     }
   }

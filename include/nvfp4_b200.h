@@ -68,7 +68,8 @@ typedef struct nvfp4_options {
    *   C[m, n] = act(acc[m, n] + bias[n]), rounded to the output type. */
   const float* bias;              /* NULL, or N fp32 values (device), the same for every batch */
   int activation;                 /* 0 = none, 1 = relu, 2 = gelu (erf form) */
-  int out_dtype;                  /* 0 = fp16, 1 = bf16 (c holds bf16) */
+  int out_dtype;                  /* 0 = fp16, 1 = bf16, 2 = fp32 (c holds that type; fp32:
+                                     dense plain schedule, not with stream_k) */
 } nvfp4_options;
 
 /* Human-readable message for the last error returned on this thread. */

@@ -209,12 +209,12 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   return e;
 }
 
-template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false, bool SK = false>
+template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false, bool SK = false, bool F32 = false>
 int launch(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tsp,
            const CUtensorMap& tsq, const GemmParams& prm, int grid,
            cudaStream_t stream) {
   using C_ = Cfg<BN, KB, CTA2>;
-  auto kern = nvfp4_gemm_kernel<GROUPED, SWAP, BN, KB, CTA2, SK>;
+  auto kern = nvfp4_gemm_kernel<GROUPED, SWAP, BN, KB, CTA2, SK, F32>;
   static bool attr_done[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -414,6 +414,10 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
       prm.sk_ktn = 0;
     }
   }
+  if (opt && opt->out_dtype == 2) {
+    if constexpr (CTA2) return fail(NVFP4_ERR_UNSUPPORTED, "fp32 C is not built for CTA pairs");
+    else return launch<false, SWAP, BN, KB, false, false, true>(tp, tq, tsp, tsq, prm, grid, stream);
+  }
   return launch<false, SWAP, BN, KB, CTA2>(tp, tq, tsp, tsq, prm, grid, stream);
 }
 
@@ -605,8 +609,12 @@ int nvfp4_gemm_ex(const void* a, const void* b, const void* sfa_perm, const void
     return fail(NVFP4_ERR_ALIGNMENT, "a, b and the scale tensors must be 16-byte aligned");
   if ((reinterpret_cast<uintptr_t>(c) & 1u) != 0)
     return fail(NVFP4_ERR_ALIGNMENT, "c must be 2-byte aligned");
-  if (opt && (opt->activation < 0 || opt->activation > 2 || opt->out_dtype < 0 || opt->out_dtype > 1))
-    return fail(NVFP4_ERR_INVALID_ARG, "activation must be 0..2 and out_dtype 0..1");
+  if (opt && (opt->activation < 0 || opt->activation > 2 || opt->out_dtype < 0 || opt->out_dtype > 2))
+    return fail(NVFP4_ERR_INVALID_ARG, "activation must be 0..2 and out_dtype 0..2");
+  if (opt && opt->out_dtype == 2 && (reinterpret_cast<uintptr_t>(c) & 3u) != 0)
+    return fail(NVFP4_ERR_ALIGNMENT, "an fp32 c must be 4-byte aligned");
+  if (opt && opt->out_dtype == 2 && opt->stream_k == 2)
+    return fail(NVFP4_ERR_UNSUPPORTED, "stream-K stores fp16 or bf16 only");
   if (opt && opt->bias && (reinterpret_cast<uintptr_t>(opt->bias) & 3u) != 0)
     return fail(NVFP4_ERR_ALIGNMENT, "bias must be 4-byte aligned");
   DeviceState* st = nullptr;

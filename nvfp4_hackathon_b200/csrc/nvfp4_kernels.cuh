@@ -324,9 +324,13 @@ __device__ __forceinline__ uint32_t epi_pack(const GemmParams& prm, float x, flo
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// SK: stream-K schedule (dense, BN <= 128); a separate instantiation so that the plain
-// schedule's code is not touched by it.
-template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false, bool SK = false>
+// (The F32 and SK instantiations leave parts of the shared epilogue unreachable: the packed
+// fp16 loop after the fp32 path's `continue`, and the stream-K `store_tile` label.)
+#pragma nv_diagnostic push
+#pragma nv_diag_suppress 128, 177
+// SK: stream-K schedule (dense, BN <= 128); F32: fp32 C (dense).  Separate instantiations,
+// so that the plain fp16 schedule's code and register allocation are not touched by them.
+template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false, bool SK = false, bool F32 = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
 nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constant__ CUtensorMap tm_q,
                   const __grid_constant__ CUtensorMap tm_sfp, const __grid_constant__ CUtensorMap tm_sfq,
@@ -864,6 +868,57 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           goto store_tile;
         }
       }
+      if constexpr (F32) {
+        {
+          // fp32 C: the 32-bit values would double the packed tile's registers, so each
+          // 16-column piece is stored straight from its TMEM load and the accumulator is
+          // released after the last store.
+          float* const Cf = reinterpret_cast<float*>(prm.C) + (long long)ti.l * prm.c_batch;
+          const int p = ti.p0 + row;
+#pragma unroll 1
+          for (int c = 0; c < kChunks; ++c) {
+            if (q_lo + c * 32 >= ti.q_rows) break;  // warp-uniform
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+              uint32_t r[16];
+              tmem_ld_32x32b_x16(t_row + c * 32 + hh * 16, r);
+              tmem_ld_wait();
+              const int qb = q_lo + c * 32 + hh * 16;
+              float v[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = epi_post(prm, __uint_as_float(r[j]), SWAP ? p : qb + j, ncols);
+              if (p >= ti.p_rows) continue;
+              if constexpr (!SWAP) {
+                float* dst = Cf + (long long)p * ti.ldc + qb;
+                if (qb + 16 <= ti.q_rows && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+                  for (int w = 0; w < 4; ++w)
+                    reinterpret_cast<float4*>(dst)[w] = make_float4(v[4 * w], v[4 * w + 1], v[4 * w + 2], v[4 * w + 3]);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j)
+                    if (qb + j < ti.q_rows) dst[j] = v[j];
+                }
+              } else {
+                // D[p=n, q=m] -> C[m, n]: lanes hold consecutive n (coalesced per j)
+                float* dst = Cf + (long long)qb * ti.ldc + p;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                  if (qb + j < ti.q_rows) dst[(long long)j * ti.ldc] = v[j];
+              }
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) arrive_leader(acce_bar(acc));
+          if (++acc == A) { acc = 0; aph ^= 1; }
+          if (threadIdx.x == 0) {
+            if (etile == 0) trace_cta(prm, 2);
+            trace_event(tsm, 5, etile++ - tbase / 32u);
+          }
+          continue;
+        }
+      }
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
         if (q_lo + c * 32 < ti.q_rows && !(prm.debug & 64)) {  // warp-uniform
@@ -961,5 +1016,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     else tmem_dealloc(tmem_base, C_::kTmemCols);
   }
 }
+
+#pragma nv_diagnostic pop
 
 }  // namespace nvfp4

@@ -24,6 +24,8 @@ _compiled = None
 # checks.  Bounded, and holds no strong references.
 _validated: dict = {}
 _VALIDATED_MAX = 32
+# output dtype of C -> the options' out_dtype
+_OUT_DTYPES = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 
 
 def compile_kernel():
@@ -70,8 +72,8 @@ def _validate(a, b, sfa_perm, sfb_perm, c):
     k = 2 * kb  # two e2m1 values per byte (submission.py:779)
     _check_operand(a, m, kb, l, "a")
     _check_operand(b, n, kb, l, "b")
-    if c.dtype not in (torch.float16, torch.bfloat16) or tuple(c.shape) != (m, n, l):
-        raise ValueError(f"c must be float16 (or bfloat16) of shape {(m, n, l)}")
+    if c.dtype not in _OUT_DTYPES or tuple(c.shape) != (m, n, l):
+        raise ValueError(f"c must be float16 (or bfloat16, float32) of shape {(m, n, l)}")
     if any(sz > 1 and st != w for sz, st, w in zip(c.shape, c.stride(), (n, 1, m * n))):
         raise ValueError(f"c must have strides {(n, 1, m * n)}; got {c.stride()}")
     sf_k = ceil_div(k, SF_VEC)
@@ -92,10 +94,11 @@ def custom_kernel(data: gemm_input_t, opt: _native.Nvfp4Options | None = None) -
             _validated.clear()
         _validated[key] = (tuple(weakref.ref(t) for t in (a, b, sfa_perm, sfb_perm, c)), (m, n, k, l))
     lib = _native.load()
-    if opt is None and c.dtype == torch.bfloat16:
-        opt = _native.options(out_dtype=1)
-    elif opt is not None and c.dtype == torch.bfloat16 and opt.out_dtype != 1:
-        raise ValueError("c is bfloat16 but opt.out_dtype is not 1")
+    want = _OUT_DTYPES[c.dtype]
+    if opt is None and want:
+        opt = _native.options(out_dtype=want)
+    elif opt is not None and opt.out_dtype != want:
+        raise ValueError(f"c is {c.dtype} but opt.out_dtype is {opt.out_dtype} (expected {want})")
     if opt is None:
         rc = lib.nvfp4_gemm(a.data_ptr(), b.data_ptr(), sfa_perm.data_ptr(), sfb_perm.data_ptr(),
                             c.data_ptr(), m, n, k, l, _current_stream(a))
@@ -115,7 +118,8 @@ def fused(data: gemm_input_t, bias: torch.Tensor | None = None, activation: str 
     """``custom_kernel`` with a fused epilogue: C = act(A B^T + bias) in C's dtype.
 
     bias: None or an fp32 CUDA vector of N values (one per output column, shared by all
-    batches); activation: None, "relu" or "gelu" (erf form); c may be float16 or bfloat16.
+    batches); activation: None, "relu" or "gelu" (erf form); c may be float16, bfloat16 or
+    float32.
     The bias and activation are applied to the fp32 accumulator before the rounding, as a
     cuBLASLt bias/relu epilogue does.
     """
@@ -130,5 +134,5 @@ def fused(data: gemm_input_t, bias: torch.Tensor | None = None, activation: str 
         opt = _native.options()
     opt.bias = bias.data_ptr() if bias is not None else None
     opt.activation = _ACTIVATIONS[activation]
-    opt.out_dtype = 1 if c.dtype == torch.bfloat16 else 0
+    opt.out_dtype = _OUT_DTYPES.get(c.dtype, 0)
     return custom_kernel(data, opt=opt)

@@ -1,4 +1,4 @@
-"""Fused epilogue of the dense GEMM (bias per output column, relu / gelu, fp16 or bf16 C)
+"""Fused epilogue of the dense GEMM (bias per output column, relu / gelu, fp16, bf16 or fp32 C)
 against the oracle's float64 product with the same epilogue applied before rounding."""
 import math
 
@@ -32,7 +32,7 @@ def _act(x, name):
 
 @pytest.mark.parametrize("m,n,k,l", [(64, 384, 1024, 1), (256, 640, 512, 2), (128, 1536, 7168, 1)])
 @pytest.mark.parametrize("activation", [None, "relu", "gelu"])
-@pytest.mark.parametrize("out", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("out", [torch.float16, torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_fused_epilogue(cuda, m, n, k, l, activation, out, with_bias):
     data = list(inputs.generate_input(m, n, k, l, seed=21))
@@ -47,7 +47,7 @@ def test_fused_epilogue(cuda, m, n, k, l, activation, out, with_bias):
         exp = exp + bias.double().cpu().numpy()[None, None, :]
     exp = torch.from_numpy(_act(exp, activation)).to(out).double().numpy()
     got = c.permute(2, 0, 1).double().cpu().numpy()
-    tol = 1e-3 if out == torch.float16 else 8e-3  # one ulp of the output type
+    tol = 8e-3 if out == torch.bfloat16 else 1e-3  # one ulp of bf16; the reference checker's 1e-3 otherwise
     bad = np.abs(got - exp) > tol + tol * np.abs(exp)
     assert not bad.any(), f"{bad.sum()} mismatches, max err {np.abs(got - exp).max()}"
 
@@ -68,3 +68,27 @@ def test_grouped_rejects_fused_options(cuda):
     import ctypes
     rc = lib.nvfp4_grouped_gemm_ex(16, 16, 16, 1, 16, 1 << 20, None, ctypes.byref(opt))
     assert rc == 3  # NVFP4_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("m,n,k,l", [(64, 384, 1024, 1), (200, 520, 512, 2), (300, 2304, 2048, 1)])
+def test_fp32_output_through_custom_kernel(cuda, m, n, k, l):
+    """fp32 C: every tile config (swap for M <= 128, 256-wide tiles for N >= 2048), ragged
+    edges, batches; compared with the exact product at the reference checker's tolerance."""
+    data = list(inputs.generate_input(m, n, k, l, seed=4))
+    data[6] = torch.full((l, m, n), float("nan"), device="cuda", dtype=torch.float32).permute(1, 2, 0)
+    c = gemm.custom_kernel(tuple(data))
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
+    exp = _exact(data)
+    got = c.permute(2, 0, 1).double().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert np.allclose(got, exp, rtol=1e-3, atol=1e-3)
+    # fp32 keeps what fp16 rounds away
+    assert np.abs(got - exp).max() < np.abs(exp.astype(np.float16).astype(np.float64) - exp).max()
+
+
+def test_fp32_output_rejects_stream_k(cuda):
+    data = list(inputs.generate_input(128, 256, 512, 1, seed=2))
+    data[6] = torch.zeros((1, 128, 256), device="cuda", dtype=torch.float32).permute(1, 2, 0)
+    with pytest.raises(RuntimeError):
+        gemm.custom_kernel(tuple(data), opt=_native.options(out_dtype=2, stream_k=2))

@@ -4,8 +4,8 @@ The 20-warp block gets at most 96 registers per thread. A change to the epilogue
 the packed accumulator tile live across a loop back-edge once pushed every plain
 instantiation into local memory (up to 1.7 KB of spills per thread) and cost 10-130 % in
 run time without changing any result, so only a compile-time check sees it. The plain
-schedule (SK = false) and the quantiser must not spill; the opt-in stream-K instantiations
-are allowed to.
+schedule (SK = false, fp16/bf16 or fp32 C) and the quantiser must not spill; the opt-in
+stream-K instantiations are allowed to.
 """
 import os
 import re
@@ -45,8 +45,8 @@ def test_plain_kernels_do_not_spill(tmp_path):
     report = _ptxas_report(tmp_path)
     gemms = [r for r in report if "nvfp4_gemm_kernel" in r[0]]
     assert gemms, "no GEMM instantiation found in the ptxas report"
-    # mangled template arguments end in ...ELb<CTA2>ELb<SK>EEEv
-    plain = [r for r in gemms if re.search(r"ELb[01]ELb0EEEv", r[0])]
+    # mangled template arguments end in ...ELb<CTA2>ELb<SK>ELb<F32>EEEv
+    plain = [r for r in gemms if re.search(r"ELb[01]ELb0ELb[01]EEEv", r[0])]
     assert plain
     bad = [r for r in plain + [r for r in report if "quantize" in r[0]] if r[2] != 0]
     assert not bad, "spilling instantiations: " + "; ".join(f"{n[-48:]} {g} regs {s} B" for n, g, s in bad)

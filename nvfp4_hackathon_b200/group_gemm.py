@@ -20,7 +20,7 @@ from . import _native
 from .layout import SF_VEC, ceil_div, is_permuted_layout
 from .task import group_input_t, group_output_t
 
-_TABLE_CACHE: "OrderedDict[tuple, torch.Tensor]" = OrderedDict()
+_TABLE_CACHE: "OrderedDict[tuple, tuple[torch.Tensor, torch.Tensor]]" = OrderedDict()  # (device, pinned source)
 _TABLE_CACHE_MAX = 64
 _WORKSPACES: dict[tuple, torch.Tensor] = {}
 
@@ -36,10 +36,10 @@ def _table(abc, sfp, sizes, device) -> torch.Tensor:
     key = (device.index,) + tuple(
         (a.data_ptr(), b.data_ptr(), c.data_ptr(), sa.data_ptr(), sb.data_ptr()) + tuple(sz)
         for (a, b, c), (sa, sb), sz in zip(abc, sfp, sizes))
-    t = _TABLE_CACHE.get(key)
-    if t is not None:
+    hit = _TABLE_CACHE.get(key)
+    if hit is not None:
         _TABLE_CACHE.move_to_end(key)
-        return t
+        return hit[0]
     G = len(sizes)
     host = torch.empty(7 * G, dtype=torch.int64, pin_memory=True)
     sz32 = host[: 2 * G].view(torch.int32)
@@ -49,7 +49,9 @@ def _table(abc, sfp, sizes, device) -> torch.Tensor:
     host[5 * G: 7 * G] = torch.tensor([[sa.data_ptr(), sb.data_ptr()] for sa, sb in sfp],
                                       dtype=torch.int64).reshape(-1)
     t = host.to(device, non_blocking=True)
-    _TABLE_CACHE[key] = t
+    # the pinned source stays with the table: a copy captured into a CUDA graph re-reads
+    # it on every replay
+    _TABLE_CACHE[key] = (t, host)
     if len(_TABLE_CACHE) > _TABLE_CACHE_MAX:
         _TABLE_CACHE.popitem(last=False)
     return t

@@ -7,9 +7,10 @@
 //                                                                out of range -> NaN)
 //   v       = x / float(scale_b)   (correctly rounded; 0 when the scale is 0)
 //   code    = nearest e2m1 of min(|v|, 6), ties to the even code; sign bit on non-zero codes
-// The code comes from the hardware conversion cvt.rn.satfinite.e2m1x2.f32 (round to nearest,
-// ties to even on the e2m1 grid, saturating at 6), with the -0 it gives for small negative
-// values cleared to 0.
+// v is formed exactly with one multiply and two fmas (Markstein's correction step, see
+// quotient_rn); the code comes from the hardware conversion cvt.rn.satfinite.e2m1x2.f32
+// (round to nearest, ties to even on the e2m1 grid, saturating at 6), with the -0 it gives
+// for small negative values cleared to 0.
 // Element 2i of a row goes to the low nibble of byte i.
 //
 // Layout of the permuted scales (kernels/gemm/reference.py:113-150): per 128-row block and
@@ -76,25 +77,30 @@ constexpr int kQuantBatch = 4;   // rows whose loads a warp keeps in flight toge
 template <int DT> __host__ __device__ constexpr int quant_epl() { return DT == kQuantF32 ? 8 : 16; }
 template <int DT> __host__ __device__ constexpr int quant_atoms() { return quant_epl<DT>() / 2; }  // atoms per CTA
 
-// Codes of 8 elements (half a block) given the block's scale; returns 4 packed bytes.
-// The definition rounds the correctly rounded v = x / s.  q = x * (1 / s) is within ~1 ulp
-// of x / s, so both x / s and its rounding lie in [q (1 - 2^-21), q (1 + 2^-21)]; the
-// conversion is monotone, so where it agrees at both ends of that interval its result is
-// exact, and only a pair that straddles a rounding boundary pays for the division.
+// Codes of 8 elements (half a block) given the block's scale and its correctly rounded
+// reciprocal inv = RN(1/s); returns 4 packed bytes.  The definition rounds the correctly
+// rounded quotient v = RN(x / s).  It is formed with Markstein's correction step
+// (P. Markstein, IBM J. Res. Dev. 34(1), 1990; J.-M. Muller et al., Handbook of
+// Floating-Point Arithmetic, the theorem on division with a correctly rounded reciprocal):
+//   q = RN(x * inv)            within one ulp of x / s
+//   r = RN(x - q * s)          exact (one fma), since q is that close
+//   v = RN(q + r * inv)        = RN(x / s)
+// The theorem needs a normal quotient; any |x / s| below the first e2m1 threshold (0.25)
+// gives code 0 whether or not it is exact, and the block's amax bounds |x / s| near 6,
+// so every quotient that decides a code is in range.  No branch, one conversion per pair.
 // Negative values that round to zero keep code 0 (the conversion would give -0).
-__device__ __forceinline__ uint32_t e2m1_pack8(const float (&v)[8], float s) {
+__device__ __forceinline__ float quotient_rn(float x, float s, float inv) {
+  const float q = __fmul_rn(x, inv);
+  const float r = __fmaf_rn(-q, s, x);
+  return __fmaf_rn(r, inv, q);
+}
+
+__device__ __forceinline__ uint32_t e2m1_pack8(const float (&v)[8], float s, float inv) {
   uint32_t w = 0;
   if (s > 0.f) {
-    const float inv = 1.0f / s;
-    constexpr float kLo = 1.0f - 4.76837158203125e-07f, kHi = 1.0f + 4.76837158203125e-07f;  // 1 -+ 2^-21
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float a = v[2 * i] * inv, b = v[2 * i + 1] * inv;
-      uint32_t c = cvt_e2m1x2(a * kLo, b * kLo);
-      if (c != cvt_e2m1x2(a * kHi, b * kHi))
-        c = cvt_e2m1x2(__fdiv_rn(v[2 * i], s), __fdiv_rn(v[2 * i + 1], s));
-      w |= c << (8 * i);
-    }
+    for (int i = 0; i < 4; ++i)
+      w |= cvt_e2m1x2(quotient_rn(v[2 * i], s, inv), quotient_rn(v[2 * i + 1], s, inv)) << (8 * i);
   }
   const uint32_t zero = ~(w | (w >> 1) | (w >> 2)) & 0x11111111u;  // magnitude-0 nibbles
   return w & ~(zero << 3);
@@ -155,18 +161,19 @@ nvfp4_quantize_kernel(const void* __restrict__ x, int rows, int k, uint8_t* __re
       if (row >= rows || !lane_ok) continue;
       const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(__fdiv_rn(amax, 6.0f), __NV_NOSAT, __NV_E4M3);
       const float s = float(*reinterpret_cast<const __nv_fp8_e4m3*>(&s8));
+      const float inv = s > 0.f ? __frcp_rn(s) : 0.f;  // correctly rounded 1 / s
       const long long rowbase = (long long)l * rows + row;
       uint8_t* cdst = codes + (rowbase * k + col) / 2;
       if constexpr (EPL == 16) {
         float lo[8], hi[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) { lo[i] = v[i]; hi[i] = v[8 + i]; }
-        *reinterpret_cast<uint2*>(cdst) = make_uint2(e2m1_pack8(lo, s), e2m1_pack8(hi, s));
+        *reinterpret_cast<uint2*>(cdst) = make_uint2(e2m1_pack8(lo, s, inv), e2m1_pack8(hi, s, inv));
       } else {
         float h[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) h[i] = v[i];
-        *reinterpret_cast<uint32_t*>(cdst) = e2m1_pack8(h, s);
+        *reinterpret_cast<uint32_t*>(cdst) = e2m1_pack8(h, s, inv);
       }
       if (writer) {
         atoms[atom * 512 + (r & 31) * 16 + (r >> 5) * 4 + j] = (uint8_t)s8;

@@ -55,6 +55,40 @@ def test_quantize_ties_zeros_and_signs(cuda):
     _check_exact(x)
 
 
+def _boundary_rows():
+    """Rows of 64 values: per block, amax = 6 s (so the block's scale is exactly s) and 15
+    values at and within two fp32 ulps of s times each e2m1 decision threshold, both signs,
+    for every positive finite e4m3 scale s (normal and subnormal)."""
+    s_vals = torch.arange(1, 127, dtype=torch.uint8).view(torch.float8_e4m3fn).float().tolist()
+    thresholds = [0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0]
+    blocks = []
+    for sv in s_vals:
+        vals = []
+        for t in thresholds:
+            base = torch.tensor(t * sv, dtype=torch.float32)
+            around = [base]
+            lo = hi = base
+            for _ in range(2):
+                lo = torch.nextafter(lo, torch.tensor(-float("inf")))
+                hi = torch.nextafter(hi, torch.tensor(float("inf")))
+                around += [lo, hi]
+            for v in around:
+                vals += [float(v), -float(v)]
+        for i in range(0, len(vals), 15):
+            chunk = vals[i:i + 15]
+            blocks.append([6.0 * sv] + chunk + [0.0] * (15 - len(chunk)))
+    while len(blocks) % 4:
+        blocks.append([0.0] * 16)
+    return torch.tensor(blocks, dtype=torch.float32).reshape(1, -1, 64)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_quantize_rounding_boundaries(cuda, dtype):
+    x = _boundary_rows().to("cuda")
+    _check_exact(x.to(dtype))
+
+
 @pytest.mark.gpu
 def test_quantize_feeds_the_gemm(cuda):
     m, n, k = 192, 384, 1024

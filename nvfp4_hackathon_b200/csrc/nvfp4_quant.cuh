@@ -108,7 +108,7 @@ __device__ __forceinline__ uint32_t e2m1_pack8(const float (&v)[8], float s, flo
 
 // (4 CTAs of 8 warps per SM: other warps' loads cover a warp's compute phase)
 template <int DT>
-__global__ void __launch_bounds__(256, DT == kQuantBF16 ? 3 : 4)
+__global__ void __launch_bounds__(256, 4)
 nvfp4_quantize_kernel(const void* __restrict__ x, int rows, int k, uint8_t* __restrict__ codes,
                       uint8_t* __restrict__ sf_perm, uint8_t* __restrict__ sf_plain) {
   constexpr int EPL = quant_epl<DT>();
@@ -159,7 +159,10 @@ nvfp4_quantize_kernel(const void* __restrict__ x, int rows, int k, uint8_t* __re
       for (int i = 0; i < EPL; ++i) amax = fmaxf(amax, fabsf(v[i]));
       if constexpr (EPL == 8) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       if (row >= rows || !lane_ok) continue;
-      const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(__fdiv_rn(amax, 6.0f), __NV_NOSAT, __NV_E4M3);
+      // amax / 6 correctly rounded (1.0f / 6.0f folds to RN(1/6) at compile time; a
+      // quotient too small for the correction step's theorem is below e4m3's range and
+      // becomes scale 0 either way)
+      const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(quotient_rn(amax, 6.0f, 1.0f / 6.0f), __NV_NOSAT, __NV_E4M3);
       const float s = float(*reinterpret_cast<const __nv_fp8_e4m3*>(&s8));
       const float inv = s > 0.f ? __frcp_rn(s) : 0.f;  // correctly rounded 1 / s
       const long long rowbase = (long long)l * rows + row;

@@ -4,12 +4,15 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1] [--impl ours|reference]
 
 One "step" is one call of the hot path over one batch of synthetic input.
-Default workload: configs[1] of BASELINE.json (M=64, N=14336, K=4096, L=1), one
-replica per GPU (the dense GEMM does not shard; scaling "weak").  Other
-workloads: c0, c2 (dense), c3 (grouped G=8), c4a (grouped G=64, experts sharded
-across ranks, strong scaling), c4b (dense 16384x28672x8192 sharded along N,
-strong scaling; ``--gather`` gives every rank the whole C with an NCCL all-gather, or with
-``--gather p2p`` by the GEMM's own epilogue storing into every rank's C over NVLink).
+Default workload: configs[4b] of BASELINE.json, the largest configuration that
+fits one GPU: the dense GEMM M=16384, N=28672, K=8192, sharded along N over the
+ranks (strong scaling: the same total work at every N).  ``value`` is the
+GEMM-only throughput; at N > 1 the line also reports the NCCL all-gather that
+would give one rank the whole C (``gather_ms``, ``gather_gbs``), timed as its own
+leg.  ``--gather`` puts the all-gather inside every step instead (``--gather p2p``:
+the GEMM's own epilogue stores into every rank's C over NVLink).  Other workloads:
+c0, c1, c2 (dense replicas, weak scaling), c3 (grouped G=8, replicas), c4a (grouped
+G=64, experts sharded across ranks, strong scaling).
 
 Prints one JSON line on rank 0.  ``value`` is the kernel throughput with inputs
 resident in HBM: the K steps rotate over enough input copies that they never hit
@@ -56,7 +59,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--config", default="c1", choices=sorted(WORKLOADS))
+    ap.add_argument("--config", default="c4b", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", nargs="?", const="nccl", default=None, choices=["nccl", "p2p"],
                     help="c4b: every rank gets the whole C: nccl (default) = GEMM + NCCL all-gather; "
@@ -341,7 +344,9 @@ def bench_ours(args):
         t1e.record(stream)
         torch.cuda.synchronize()
         first_ms = t0e.elapsed_time(t1e)
-        reps = max(1, min(200, int(300.0 / max(first_ms, 1e-3))))
+        # >= 1 s of timed replays, so the clock sampler sees >= 10 samples under load
+        reps = max(1, min(20000, -(-1000.0 // max(first_ms, 1e-3))))
+        reps = int(reps)
         barrier()
         t0e.record(stream)
         for _ in range(reps):
@@ -357,6 +362,36 @@ def bench_ours(args):
     total_ms = float(t.item())
     _native.raise_on_device_error()
     del graph
+
+    # ------------------------------------------------- all-gather leg (c4b, N > 1, not in the step)
+    gather_leg = None
+    if wl.kind == "dense_sharded" and world > 1 and not args.gather:
+        from nvfp4_hackathon_b200 import sharding
+        w = WORKLOADS[args.config]
+        m_full, n_full = w["m"], w["n"]
+        lo0, hi0 = sharding.column_shard(n_full, world, 0)
+        shard = wl.data[6][:, :, 0]
+        gathered = torch.empty((world, m_full, hi0 - lo0), dtype=torch.float16, device=device)
+        for _ in range(3):
+            sharding.gather_columns(shard, gathered, dist)
+        barrier()
+        g_steps = max(3, min(args.steps, 20))
+        gs, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        gs.record(stream)
+        for _ in range(g_steps):
+            sharding.gather_columns(shard, gathered, dist)
+        ge.record(stream)
+        barrier()
+        t = torch.tensor([gs.elapsed_time(ge) / g_steps], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        g_ms = float(t.item())
+        g_bytes = gathered.numel() * gathered.element_size()
+        gather_leg = {"gather_ms": round(g_ms, 4),
+                      "gather_gbs": round(g_bytes / (g_ms * 1e-3) / 1e9, 1),
+                      "gather": f"NCCL all_gather_into_tensor of the fp16 column shards into "
+                                f"({world}, {m_full}, {hi0 - lo0}) on every rank, {g_steps} calls timed "
+                                f"on their own (not inside the GEMM step); gbs = gathered bytes / time"}
+        del gathered
 
     # ---------------------------------------------------------------- e2e (host buffers)
     e2e_steps = args.e2e_steps or min(args.steps, 50)
@@ -438,6 +473,8 @@ def bench_ours(args):
             "gpu_launches": wl.launches_per_step * (args.steps * reps + e2e_steps),
             "clocks": sampler.summary(t_wall0, t_wall1),
         }
+        if gather_leg:
+            line.update(gather_leg)
         if world == 1:
             line["cpu_baseline"] = cpu_baseline(args, wl)
         print(json.dumps(line), flush=True)

@@ -16,8 +16,9 @@
  * Every entry point launches on the given CUDA stream (cudaStream_t passed
  * as void*, NULL = legacy default stream) and never synchronises it.  Return
  * value 0 = launched; otherwise an NVFP4_ERR_* code, with a message from
- * nvfp4_last_error().  Device-side failures (a pipeline wait that ran out)
- * are recorded in a per-device status word: see nvfp4_status_get().
+ * nvfp4_last_error().  Device-side failures (a pipeline wait that ran out,
+ * a bad group entry) are recorded in a per-device status word (see
+ * nvfp4_status_get()), or in the caller's own word (nvfp4_options.dev_status).
  */
 #ifndef NVFP4_B200_H
 #define NVFP4_B200_H
@@ -29,7 +30,7 @@
 extern "C" {
 #endif
 
-#define NVFP4_ABI_VERSION 1
+#define NVFP4_ABI_VERSION 2
 
 #define NVFP4_OK 0
 #define NVFP4_ERR_INVALID_ARG 1   /* null pointer, non-positive size, bad group table */
@@ -54,16 +55,19 @@ typedef struct nvfp4_options {
   int tile_n;                     /* 0 = auto; else 64, 128 or 256 */
   int max_ctas;                   /* 0 = one CTA per SM */
   unsigned long long timeout_ns;  /* 0 = library default (2 s per pipeline wait) */
-  int debug;                      /* test/probe bits, 0 in normal use: 1 = issue no loads so every
-                                     pipeline wait runs out (status test); 2/4/8/16 = skip data
-                                     movement / MMAs / scale stores / output stores (timing probes) */
-  void* trace;                    /* NULL, or device buffer of 2 x 8 x 32 uint64 stamps (CTAs 0, 1; low 32 bits of the ns timer),
-                                     followed by 4 stamps per CTA (entry, start, first tile, exit) */
+  int debug;                      /* test bit, 0 in normal use: 1 = issue no loads, so every
+                                     pipeline wait runs out (the timeout path's test) */
+  int* dev_status;                /* NULL = record device-side errors in the per-device status
+                                     word (nvfp4_status_get); else a device int of the caller's
+                                     that this call's kernels record their first error into
+                                     (atomicCAS from 0: the caller clears it before the call) */
   int stage_k;                    /* 0 = auto; 128 or 256 K elements per pipeline stage */
   int cta_pair;                   /* 0 = auto, 1 = off, 2 = M=256 tiles on a CTA pair (cta_group::2) */
   int stream_k;                   /* dense: 0 / 1 = off, 2 = on (k-steps split evenly over all SMs).  Stream-K
-                                     keeps a small per-stream workspace (flags + fp32 partials,
-                                     ~16 MiB) allocated on first use outside stream capture */
+                                     keeps a per-stream workspace (flags + fp32 partials, ~16 MiB),
+                                     allocated by the first stream-K call on that stream (outside
+                                     any capture of it); its flags are cleared by a memset on the
+                                     stream before every stream-K launch */
   /* Fused epilogue, dense GEMM only (the grouped entry points reject it):
    *   C[m, n] = act(acc[m, n] + bias[n]), rounded to the output type. */
   const float* bias;              /* NULL, or N fp32 values (device), the same for every batch */

@@ -60,7 +60,7 @@ class Nvfp4Options(ctypes.Structure):
         ("max_ctas", ctypes.c_int),
         ("timeout_ns", ctypes.c_ulonglong),
         ("debug", ctypes.c_int),
-        ("trace", ctypes.c_void_p),
+        ("dev_status", ctypes.c_void_p),
         ("stage_k", ctypes.c_int),
         ("cta_pair", ctypes.c_int),
         ("stream_k", ctypes.c_int),
@@ -151,7 +151,9 @@ def raise_on_device_error() -> None:
         raise Nvfp4Error(f"device-side error: {STATUS.get(s, s)}")
 
 
-def options(operand_order=0, tile_n=0, max_ctas=0, timeout_ns=0, debug=0, trace=None, stage_k=0,
+def options(operand_order=0, tile_n=0, max_ctas=0, timeout_ns=0, debug=0, dev_status=None, stage_k=0,
             cta_pair=0, stream_k=0, bias=None, activation=0, out_dtype=0):
-    return Nvfp4Options(operand_order, tile_n, max_ctas, timeout_ns, debug, trace, stage_k, cta_pair,
-                        stream_k, bias, activation, out_dtype)
+    """Options for the ``*_ex`` entry points; ``dev_status``: device address of an int32 that
+    receives this call's device-side error code instead of the per-device status word."""
+    return Nvfp4Options(operand_order, tile_n, max_ctas, timeout_ns, debug, dev_status, stage_k,
+                        cta_pair, stream_k, bias, activation, out_dtype)

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -58,7 +59,7 @@ struct DeviceState {
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-unsigned long long g_timeout_ns = kDefaultTimeoutNs;
+std::atomic<unsigned long long> g_timeout_ns{kDefaultTimeoutNs};
 
 int device_state(DeviceState** out) {
   int dev = 0;
@@ -215,19 +216,16 @@ int launch(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tsp,
            cudaStream_t stream) {
   using C_ = Cfg<BN, KB, CTA2>;
   auto kern = nvfp4_gemm_kernel<GROUPED, SWAP, BN, KB, CTA2, SK, F32>;
-  static bool attr_done[kMaxDevices] = {};
+  // the shared-memory opt-in is per device and per kernel; concurrent host threads may
+  // race to set it, which is harmless (same value), but the flag itself is atomic
+  static std::atomic<bool> attr_done[kMaxDevices];
   int dev = 0;
   cudaGetDevice(&dev);
-  // tracing (a debug option) stages its stamps in extra shared memory
-  const int smem = C_::kSmemBytes + (prm.trace ? kTraceSmemBytes : 0);
-  if (smem > kMaxDynamicSmem) return fail(NVFP4_ERR_UNSUPPORTED, "trace does not fit this tile config");
-  if (!attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C_::kSmemBytes + kTraceSmemBytes <= kMaxDynamicSmem
-                                             ? C_::kSmemBytes + kTraceSmemBytes
-                                             : C_::kSmemBytes);
+  const int smem = C_::kSmemBytes;
+  if (!attr_done[dev].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_release);
   }
   cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kNumThreads), smem, stream,
                              CTA2 ? 2 : 1, SK, tp, tq, tsp, tsq, prm);
@@ -261,9 +259,10 @@ DenseChoice choose_dense(int m, int n, int k, const nvfp4_options* opt) {
 }
 
 // Stream-K workspace of one (device, stream): a flag per CTA (up to kSkMaxCtas) and one
-// fp32 partial tile (128 x BN) per CTA in kSkSlotsBytes.  Allocated on first use and kept;
-// none is allocated while the stream is being captured into a graph (the call then runs
-// without stream-K).
+// fp32 partial tile (128 x BN) per CTA in kSkSlotsBytes.  Allocated on first use and kept.
+// On a stream that is being captured into a graph, the one-time allocation is made outside
+// the capture (relaxed capture mode for this thread), and the graph keeps using it.  The
+// flags are cleared by a memset on the stream before every stream-K launch.
 constexpr int kSkMaxCtas = 1024;
 constexpr size_t kSkSlotsBytes = 16u << 20;
 struct SkWorkspace {
@@ -286,16 +285,11 @@ void* sk_workspace(int dev, cudaStream_t stream) {
   void* p = nullptr;
   const size_t bytes = kSkMaxCtas * sizeof(unsigned) + kSkSlotsBytes;
   if (cap == cudaStreamCaptureStatusNone) {
-    if (cudaMalloc(&p, bytes) != cudaSuccess || cudaMemset(p, 0, kSkMaxCtas * sizeof(unsigned)) != cudaSuccess) {
-      if (p) cudaFree(p);
+    if (cudaMalloc(&p, bytes) != cudaSuccess) {
       cudaGetLastError();
       return nullptr;
     }
   } else {
-    // A stream being captured into a graph: a one-time allocation, outside the capture
-    // (relaxed mode for this thread only), that the graph's launches keep using.  The
-    // flags need no clearing: the kernel clears each CTA's flag itself, and a published
-    // flag holds kSkPublished, which fresh memory does not.
     cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
     cudaThreadExchangeStreamCaptureMode(&mode);
     const cudaError_t e = cudaMalloc(&p, bytes);
@@ -366,10 +360,9 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   if (total > 0x7fffffffLL) return fail(NVFP4_ERR_UNSUPPORTED, "too many tiles");
   prm.total_tiles = (int)total;
   prm.q_fastest = 0;
-  prm.status = st->status;
-  prm.timeout_ns = (opt && opt->timeout_ns) ? opt->timeout_ns : g_timeout_ns;
-  prm.debug = opt ? opt->debug : 0;
-  prm.trace = opt ? reinterpret_cast<unsigned long long*>(opt->trace) : nullptr;
+  prm.status = (opt && opt->dev_status) ? opt->dev_status : st->status;
+  prm.timeout_ns = (opt && opt->timeout_ns) ? opt->timeout_ns : g_timeout_ns.load();
+  prm.debug = opt ? (opt->debug & 1) : 0;
   if (opt) {
     prm.bias = opt->bias;
     prm.act = opt->activation;
@@ -403,7 +396,9 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
     void* ws = (g <= kSkMaxCtas && (size_t)g * BN * 128 * sizeof(float) <= kSkSlotsBytes &&
                 (long long)prm.total_tiles * ktn < 0x7fffffffLL)
                    ? sk_workspace(dev, stream) : nullptr;
-    if (ws && g > prm.total_tiles) {
+    // every flag starts clear, whatever an earlier launch (even one that timed out) left
+    if (ws && g > prm.total_tiles &&
+        cudaMemsetAsync(ws, 0, (size_t)g * sizeof(unsigned), stream) == cudaSuccess) {
       prm.sk_ktn = ktn;
       prm.sk_flags = static_cast<unsigned*>(ws);
       prm.sk_slots = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kSkMaxCtas * sizeof(unsigned));
@@ -542,7 +537,7 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   cudaError_t e = launch_pdl(nvfp4_grouped_prep, dim3(1), dim3(threads), 0, stream, 1, false, tp, tq, sizes,
                              reinterpret_cast<const unsigned long long*>(abc),
                              reinterpret_cast<const unsigned long long*>(sfs), G, maps, prefix, BN,
-                             st->status);
+                             (opt && opt->dev_status) ? opt->dev_status : st->status);
   if (e != cudaSuccess) return cuda_fail(e, "nvfp4_grouped_prep launch");
   GemmParams prm;
   std::memset(&prm, 0, sizeof(prm));
@@ -552,10 +547,9 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   prm.sfs = reinterpret_cast<const unsigned long long*>(sfs);
   prm.maps = maps;
   prm.tile_prefix = prefix;
-  prm.status = st->status;
-  prm.timeout_ns = (opt && opt->timeout_ns) ? opt->timeout_ns : g_timeout_ns;
-  prm.debug = opt ? opt->debug : 0;
-  prm.trace = opt ? reinterpret_cast<unsigned long long*>(opt->trace) : nullptr;
+  prm.status = (opt && opt->dev_status) ? opt->dev_status : st->status;
+  prm.timeout_ns = (opt && opt->timeout_ns) ? opt->timeout_ns : g_timeout_ns.load();
+  prm.debug = opt ? (opt->debug & 1) : 0;
   int grid = st->num_sms;
   if (opt && opt->max_ctas > 0 && opt->max_ctas < grid) grid = opt->max_ctas;
   // (the grouped kernel copies scales with plain bulk copies: the scale maps are unused)

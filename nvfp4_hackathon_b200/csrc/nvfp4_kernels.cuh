@@ -62,7 +62,7 @@ constexpr int kFirstSfWarp = kMmaWarp + 1;
 constexpr int kSfGroups = 2;        // groups of 4 scale warps; group g serves k-steps j % 2 == g
 constexpr int kNumThreads = 32 * (kFirstSfWarp + 4 * kSfGroups);
 constexpr int kMaxDynamicSmem = 232448;     // opt-in dynamic shared memory per CTA on sm_100
-constexpr int kSmemBudget = kMaxDynamicSmem - 2560;  // minus alignment, barriers, trace stamps
+constexpr int kSmemBudget = kMaxDynamicSmem - 2560;  // minus alignment and barriers
 
 // KB = 64-wide K blocks per pipeline stage: 4 (256 K, one 128-byte swizzle row per
 // operand row) or 2 (128 K, 64-byte swizzle).  Smaller stages fit twice as many in
@@ -116,7 +116,7 @@ struct Cfg {
   static_assert(kStages >= kNumProducers, "need at least one stage per producer warp");
   static_assert(kColsNeeded <= 512, "TMEM budget exceeded");
   static_assert(kSfSlots <= 32, "slot bookkeeping uses 32-bit masks");
-  static_assert(kSmemBytes + 1024 <= kMaxDynamicSmem, "shared memory budget exceeded (incl. trace)");
+  static_assert(kSmemBytes + 1024 <= kMaxDynamicSmem, "shared memory budget exceeded");
 };
 
 // Everything the kernel needs; tensor maps for the dense case are separate
@@ -156,42 +156,10 @@ struct GemmParams {
   // control
   int* status;
   unsigned long long timeout_ns;
-  // Probe bits (timing experiments and the timeout test; 0 in normal use):
-  //   1 producer issues nothing (every wait must time out)   2 no data movement
-  //   4 no MMAs   8 no scale stores   16 no epilogue stores
-  // bits 20..30: first k-step of the trace window (trace only)
+  // Test bit 1: the producers issue nothing, so every pipeline wait runs out (the timeout
+  // path's test).  0 in normal use.
   int debug;
-  // When non-null, CTA 0 records %globaltimer stamps of its pipeline events here
-  // (slot layout in trace_slot()); used to measure hand-off latencies.
-  unsigned long long* trace;
 };
-
-// Trace (debug only).  When GemmParams::trace is set the kernel is launched with
-// kTraceSmemBytes of extra shared memory: every role stamps the low 32 bits of
-// %globaltimer (ns) into
-// shared memory (a global store would delay the next cluster-scope release of the
-// same thread), and at exit CTAs 0 and 1 copy their stamps to
-// trace[(cta * kTraceRoles + role) * kTraceSteps + step].  Roles:
-//   0 producer issued k-step    1 MMA wait done    2 MMA issued    3 / 4 scale group 0 / 1 done
-//   5 epilogue drained tile     6 scale warp: scales written
-//   7 last scale warp of the CTA arrived for the step
-// After those, 4 global stamps per CTA (0 entry, 1 after the wait on the previous grid,
-// 2 first accumulator drained, 3 exit).
-constexpr int kTraceSteps = 32;
-constexpr int kTraceRoles = 8;
-constexpr int kTraceSmemBytes = kTraceRoles * kTraceSteps * 4;
-constexpr int kTraceCtaBase = 2 * kTraceRoles * kTraceSteps;
-__device__ __forceinline__ void trace_cta(const GemmParams& prm, int what) {
-  if (prm.trace) prm.trace[kTraceCtaBase + 4 * blockIdx.x + what] = global_timer_ns();
-}
-__device__ __forceinline__ void trace_event(uint32_t* tsm, int role, uint32_t step) {
-  if (tsm && step < (uint32_t)kTraceSteps) tsm[role * kTraceSteps + step] = (uint32_t)global_timer_ns();
-}
-// latest of several threads' stamps (wrap-around of the 32-bit ns counter ignored)
-__device__ __forceinline__ void trace_event_max(uint32_t* tsm, int role, uint32_t step) {
-  if (tsm && step < (uint32_t)kTraceSteps)
-    atomicMax(tsm + role * kTraceSteps + step, (uint32_t)global_timer_ns());
-}
 
 // Per-tile view shared by all roles.
 struct TileInfo {
@@ -325,7 +293,7 @@ __device__ __forceinline__ uint32_t epi_pack(const GemmParams& prm, float x, flo
 }
 
 // (The F32 and SK instantiations leave parts of the shared epilogue unreachable: the packed
-// fp16 loop after the fp32 path's `continue`, and the stream-K `store_tile` label.)
+// fp16 loop after the fp32 path's `continue`.)
 #pragma nv_diagnostic push
 #pragma nv_diag_suppress 128, 177
 // SK: stream-K schedule (dense, BN <= 128); F32: fp32 C (dense).  Separate instantiations,
@@ -365,15 +333,9 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   uint8_t* bar_ptr = smem + kSlot0 + NS * C_::kSfSlotBytes;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bar_ptr + 8 * C_::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + 8 * C_::kNumBars + 4);
-  uint32_t* tsm = prm.trace ? reinterpret_cast<uint32_t*>(bar_ptr + C_::kBarrierBytes) : nullptr;
-  // the trace window starts at k-step (debug >> 20) (tiles for the epilogue role)
-  const uint32_t tbase = (uint32_t)prm.debug >> 20;
-  if (tsm)
-    for (int i = threadIdx.x; i < kTraceRoles * kTraceSteps; i += blockDim.x) tsm[i] = 0u;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) trace_cta(prm, 0);
   pdl_launch_dependents();
   // CTA pairs: rank 0 (leader) issues the MMAs for both; tiles are walked per pair.
   const uint32_t crank = CTA2 ? cluster_ctarank() : 0;
@@ -444,10 +406,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   // overlaps the previous kernel on the stream; global memory is used only after
   // that kernel has completed.
   pdl_wait_prior_grid();
-  if (threadIdx.x == 0) trace_cta(prm, 1);
-  // stream-K: this CTA's partial is not published yet (the owner of a tile also clears the
-  // flags it consumed; this covers a launch that ended early)
-  if (SK && threadIdx.x == 0) prm.sk_flags[blockIdx.x] = 0u;
+  // (stream-K: the host clears every CTA's flag before the launch)
 
   const int total = GROUPED ? __ldg(prm.tile_prefix + prm.G) : prm.total_tiles;
   const uint64_t tmo = prm.timeout_ns;
@@ -505,10 +464,6 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       uint32_t sf_issued = 0, sf_par = 0;
       auto issue_sf = [&](const Cursor& c) {
         const uint32_t bar = sfd_bar(sl);
-        if (prm.debug & 2) {  // timing probe: no data movement
-          mbar_arrive(bar);
-          return;
-        }
         const uint32_t dst = base + slot_off(sl);
         if constexpr (!GROUPED) {
           // two tensor loads (one per operand's scale blocks; out-of-range atoms read as
@@ -559,9 +514,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
             // of the scale slot step gstep + LEAD reuses)
             if (!mbar_wait_bounded(empty_bar(s), ph ^ 1, abort_flag, prm.status,
                                    kStatusTimeoutProducer, tmo)) { ok = false; break; }
-            if (prm.debug & 2) {  // timing probe: no data movement
-              mbar_arrive(full_bar(s));
-            } else {
+            {
               const uint32_t st = base + stage_off(s);
               if constexpr (CTA2) {
                 // both CTAs' tiles count on the leader's full barrier, which the MMA waits on
@@ -581,7 +534,6 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
                 issued_par = (issued_par & ~(1u << s)) | (ph << s);
               }
             }
-            trace_event(tsm, 0, gstep - tbase);
           }
           sf_step(mine);
           if (++s == S) { s = 0; ph ^= 1; }
@@ -623,8 +575,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         // (CTA-scope acquire also for the pair's barriers, which the peer arrives on: the
         // data they publish is ordered by the tcgen05 fences and the TMA transaction
         // counts, and a cluster-scope acquire costs ~0.2 us per wait)
-        if (!(prm.debug & 8192) &&
-            !mbar_wait_bounded(acce_bar(acc), aph ^ 1, abort_flag, prm.status, kStatusTimeoutMma,
+        if (!mbar_wait_bounded(acce_bar(acc), aph ^ 1, abort_flag, prm.status, kStatusTimeoutMma,
                                tmo)) { ok = false; break; }
         tc_fence_after();
         for (int kt = sg.kt0; kt < kte; ++kt, ++step) {
@@ -636,14 +587,12 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
             break;
           }
           tc_fence_after();
-          trace_event(tsm, 1, step - tbase);
           const uint32_t sfp_col = tmem_base + C_::kSfCol0 + s * C_::kSfCols;
           const uint32_t sfq_col = sfp_col + C_::kSfpCols + sfq_shift;
           const uint64_t pdesc = make_smem_desc(base + stage_off(s), 0, C_::kSbo, C_::kSwizzle);
           const uint64_t qdesc = make_smem_desc(base + stage_off(s) + kOffQ, 0, C_::kSbo, C_::kSwizzle);
           const uint32_t acc0 = kt > sg.kt0 ? 1u : 0u;
-          if (prm.debug & 4) {
-          } else if (k_blocks(ti, kt) == KB) {
+          if (k_blocks(ti, kt) == KB) {
 #pragma unroll
             for (int kb = 0; kb < KB; ++kb) {
               if constexpr (CTA2)
@@ -666,7 +615,6 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           }
           // release the stage (and its scale buffer) once these MMAs have read it
           if (CTA2) tc_commit_2cta(empty_bar(s)); else tc_commit(empty_bar(s));
-          trace_event(tsm, 2, step - tbase);
           if (++s == S) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
@@ -678,7 +626,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       mbar_wait_bounded(drain_bar, 0, abort_flag, prm.status, kStatusTimeoutDrain, tmo);
     }
   } else if (warp >= kFirstSfWarp) {
-    if (!(prm.debug & 4096)) {  // (probe bit 4096: scale warps idle)
+    {
     // -------------------------------------------------------------- scale warps
     const int grp = (warp - kFirstSfWarp) >> 2;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM quarter
@@ -747,34 +695,29 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
         if (!w_ok) { ok = false; break; }
         tc_fence_after();
-        if (!(prm.debug & 8)) {
+        {
           SfRegs r;
           load_stage(ti, kt, cslot, nq_atoms, r);
           store_stage(cs, r);
           tmem_st_wait();
         }
-        if (lane == 0 && (warp & 3) == 0) trace_event(tsm, 6, tstep - tbase);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          arrive_leader(sff_bar(cs));
-          if ((warp & 3) == 0) trace_event(tsm, 3 + grp, tstep - tbase);
-          trace_event_max(tsm, 7, tstep - tbase);
-        }
+        if (lane == 0) arrive_leader(sff_bar(cs));
       }
     }
     }
   } else {
-    if (!(prm.debug & 8192)) {  // (probe bit 8192: epilogue idle)
+    {
     // -------------------------------------------------------------- epilogue
     // Warp w owns accumulator rows 32*(w%4).. and columns [h*BN/2, (h+1)*BN/2), h = w/4.
     // It pulls its whole slice out of TMEM as packed fp16 first, releases the
     // accumulator, and only then writes global memory.
     constexpr int kHalf = BN / 2;
     constexpr int kChunks = kHalf / 32;
+    constexpr int kPhase = kChunks > 2 ? 2 : kChunks;  // chunks drained per store phase
     int acc = 0;
     uint32_t aph = 0;
-    uint32_t etile = 0;
     const int quad = warp & 3;
     const int half = warp >> 2;
     const int row = quad * 32 + lane;  // TMEM lane == accumulator row
@@ -790,7 +733,50 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       const int q_lo = ti.q0 + half * kHalf;
       const bool fused = prm.bias || prm.act || prm.out_bf16;  // (warp-uniform)
       const int ncols = SWAP ? ti.p_rows : ti.q_rows;          // output columns N
-      uint32_t pk[kChunks][16];
+      const int p = ti.p0 + row;
+      // Store chunks c0 .. c0 + kPhase - 1 (32 columns each, packed in pk) into C itself,
+      // or (n_out > 0) into every buffer of outs[].
+      auto store_c = [&](__half* const Cd, const uint32_t (&pk)[kPhase][16], int c0) {
+        if (p >= ti.p_rows) return;
+#pragma unroll
+        for (int c = 0; c < kPhase; ++c) {
+          const int qc = q_lo + (c0 + c) * 32;
+          if (qc >= ti.q_rows) break;
+          if constexpr (!SWAP) {
+            __half* dst = Cd + (long long)p * ti.ldc + qc;
+            if (qc + 32 <= ti.q_rows && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                d4[v] = make_uint4(pk[c][4 * v], pk[c][4 * v + 1], pk[c][4 * v + 2], pk[c][4 * v + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (qc + j < ti.q_rows)
+                  dst[j] = (j & 1) ? __high2half(*reinterpret_cast<const __half2*>(&pk[c][j >> 1]))
+                                   : __low2half(*reinterpret_cast<const __half2*>(&pk[c][j >> 1]));
+            }
+          } else {
+            // D[p=n, q=m] -> C[m, n]; lanes hold consecutive n, so each store is warp-coalesced
+            __half* dst = Cd + (long long)qc * ti.ldc + p;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (qc + j < ti.q_rows)
+                dst[(long long)j * ti.ldc] =
+                    (j & 1) ? __high2half(*reinterpret_cast<const __half2*>(&pk[c][j >> 1]))
+                            : __low2half(*reinterpret_cast<const __half2*>(&pk[c][j >> 1]));
+          }
+        }
+      };
+      auto store_all = [&](const uint32_t (&pk)[kPhase][16], int c0) {
+        if (prm.n_out == 0) {
+          store_c(ti.C, pk, c0);
+        } else {
+#pragma unroll
+          for (int d = 0; d < 8; ++d)
+            if (d < prm.n_out) store_c(reinterpret_cast<__half*>(prm.outs[d]), pk, c0);
+        }
+      };
       if constexpr (SK) {
         if (sg.kt0 > 0 || sg.kt1 < ti.num_kt) {
           // ---- stream-K piece of a split tile: fp32 partials meet in the owner CTA, the
@@ -856,8 +842,10 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
               }
             }
           }
+          static_assert(!SK || kPhase == kChunks, "stream-K tiles are stored in one phase");
+          uint32_t pk[kPhase][16];
 #pragma unroll
-          for (int c = 0; c < kChunks; ++c)
+          for (int c = 0; c < kPhase; ++c)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int n0 = SWAP ? ti.p0 + row : q_lo + c * 32 + 2 * j;
@@ -865,7 +853,8 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
               pk[c][j] = epi_pack(prm, epi_post(prm, a[c * 32 + 2 * j], n0, ncols),
                                   epi_post(prm, a[c * 32 + 2 * j + 1], n1, ncols));
             }
-          goto store_tile;
+          store_all(pk, 0);
+          continue;
         }
       }
       if constexpr (F32) {
@@ -912,89 +901,50 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           __syncwarp();
           if (lane == 0) arrive_leader(acce_bar(acc));
           if (++acc == A) { acc = 0; aph ^= 1; }
-          if (threadIdx.x == 0) {
-            if (etile == 0) trace_cta(prm, 2);
-            trace_event(tsm, 5, etile++ - tbase / 32u);
-          }
           continue;
         }
       }
+      // Drain kPhase chunks of 32 columns into registers as packed fp16/bf16, store them,
+      // then the next kPhase: at most 2 chunks (32 registers) are live.  The accumulator is
+      // released right after its last TMEM load; the MMAs of the next tile wait at most
+      // for the issue of the earlier phases' stores (fire-and-forget).
 #pragma unroll
-      for (int c = 0; c < kChunks; ++c) {
-        if (q_lo + c * 32 < ti.q_rows && !(prm.debug & 64)) {  // warp-uniform
+      for (int c0 = 0; c0 < kChunks; c0 += kPhase) {
+        uint32_t pk[kPhase][16];
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            uint32_t r[16];
-            tmem_ld_32x32b_x16(t_row + c * 32 + hh * 16, r);
-            tmem_ld_wait();
-            if (!fused) {
+        for (int cc = 0; cc < kPhase; ++cc) {
+          const int c = c0 + cc;
+          if (q_lo + c * 32 < ti.q_rows) {  // warp-uniform
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                __half2 h = __floats2half2_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-                pk[c][hh * 8 + j] = *reinterpret_cast<uint32_t*>(&h);
-              }
-            } else {
+            for (int hh = 0; hh < 2; ++hh) {
+              uint32_t r[16];
+              tmem_ld_32x32b_x16(t_row + c * 32 + hh * 16, r);
+              tmem_ld_wait();
+              if (!fused) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int n0 = SWAP ? ti.p0 + row : q_lo + c * 32 + hh * 16 + 2 * j;
-                const int n1 = SWAP ? n0 : n0 + 1;
-                pk[c][hh * 8 + j] = epi_pack(prm, epi_post(prm, __uint_as_float(r[2 * j]), n0, ncols),
-                                             epi_post(prm, __uint_as_float(r[2 * j + 1]), n1, ncols));
+                for (int j = 0; j < 8; ++j) {
+                  __half2 h = __floats2half2_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+                  pk[cc][hh * 8 + j] = *reinterpret_cast<uint32_t*>(&h);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const int n0 = SWAP ? ti.p0 + row : q_lo + c * 32 + hh * 16 + 2 * j;
+                  const int n1 = SWAP ? n0 : n0 + 1;
+                  pk[cc][hh * 8 + j] = epi_pack(prm, epi_post(prm, __uint_as_float(r[2 * j]), n0, ncols),
+                                                epi_post(prm, __uint_as_float(r[2 * j + 1]), n1, ncols));
+                }
               }
             }
           }
         }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) arrive_leader(acce_bar(acc));
-      if (++acc == A) { acc = 0; aph ^= 1; }
-    store_tile:
-      if (threadIdx.x == 0) {
-        if (etile == 0) trace_cta(prm, 2);
-        trace_event(tsm, 5, etile++ - tbase / 32u);
-      }
-      const int p = ti.p0 + row;
-      // C itself, or (n_out > 0) every buffer of outs[]
-      auto store_c = [&](__half* const Cd) {
-      if (p < ti.p_rows && !(prm.debug & 16)) {
-#pragma unroll
-        for (int c = 0; c < kChunks; ++c) {
-          const int qc = q_lo + c * 32;
-          if (qc >= ti.q_rows) break;
-          if constexpr (!SWAP) {
-            __half* dst = Cd + (long long)p * ti.ldc + qc;
-            if (qc + 32 <= ti.q_rows && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-              uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-              for (int v = 0; v < 4; ++v)
-                d4[v] = make_uint4(pk[c][4 * v], pk[c][4 * v + 1], pk[c][4 * v + 2], pk[c][4 * v + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (qc + j < ti.q_rows)
-                  dst[j] = (j & 1) ? __high2half(*reinterpret_cast<__half2*>(&pk[c][j >> 1]))
-                                   : __low2half(*reinterpret_cast<__half2*>(&pk[c][j >> 1]));
-            }
-          } else {
-            // D[p=n, q=m] -> C[m, n]; lanes hold consecutive n, so each store is warp-coalesced
-            __half* dst = Cd + (long long)qc * ti.ldc + p;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (qc + j < ti.q_rows)
-                dst[(long long)j * ti.ldc] =
-                    (j & 1) ? __high2half(*reinterpret_cast<__half2*>(&pk[c][j >> 1]))
-                            : __low2half(*reinterpret_cast<__half2*>(&pk[c][j >> 1]));
-          }
+        if (c0 + kPhase >= kChunks) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) arrive_leader(acce_bar(acc));
+          if (++acc == A) { acc = 0; aph ^= 1; }
         }
-      }
-      };
-      if (prm.n_out == 0) {
-        store_c(ti.C);
-      } else {
-#pragma unroll
-        for (int d = 0; d < 8; ++d)
-          if (d < prm.n_out) store_c(reinterpret_cast<__half*>(prm.outs[d]));
+        store_all(pk, c0);
       }
     }
     }
@@ -1002,10 +952,6 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) trace_cta(prm, 3);
-  if (tsm && blockIdx.x < 2)
-    for (int i = threadIdx.x; i < kTraceRoles * kTraceSteps; i += blockDim.x)
-      prm.trace[blockIdx.x * kTraceRoles * kTraceSteps + i] = tsm[i];
   // Pair: neither CTA leaves (or frees TMEM) while the leader's MMAs may still read the
   // peer's shared memory or the peer still arrives on the leader's barriers.
   if (CTA2) cluster_sync();

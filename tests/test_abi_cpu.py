@@ -20,7 +20,7 @@ def test_library_loads_and_exports():
     lib = _native.load()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.nvfp4_abi_version() == 1
+    assert lib.nvfp4_abi_version() == 2
 
 
 def test_workspace_size_is_host_only():

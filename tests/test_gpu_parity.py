@@ -132,6 +132,22 @@ def test_timeout_sets_status_and_context_survives(cuda):
     assert_close(got, dense_expected(data), "after timeout")
 
 
+def test_timeout_in_callers_status_word(cuda):
+    """opt.dev_status: the call's device-side error lands in the caller's own word and the
+    per-device word stays clear."""
+    data = inputs.generate_input(128, 256, 512, 1, seed=1)
+    a, b, _, _, sfa, sfb, c = data
+    _native.status_reset()
+    word = torch.zeros(1, dtype=torch.int32, device="cuda")
+    opt = _native.options(timeout_ns=50_000_000, debug=1, dev_status=word.data_ptr())
+    gemm.launch(a, b, sfa, sfb, c, 128, 256, 512, 1, opt=opt)
+    torch.cuda.synchronize()
+    assert int(word.item()) in (2, 3)
+    assert _native.status() == 0
+    got = _run_dense(data)
+    assert_close(got, dense_expected(data), "after timeout")
+
+
 def _grouped_expected(gdata, rows=None):
     outs = []
     for i, ((a, b, _), (sa, sb)) in enumerate(zip(gdata[0], gdata[1])):

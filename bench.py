@@ -54,12 +54,29 @@ WORKLOADS = {
 }
 
 
+# The reference's own benchmark shapes (kernels/gemm/run_tests.py:26-30 and
+# kernels/group_gemm/profile_group_gemm.py:42-83), for the same-box comparison.
+COMPARE_SETS = {
+    "ref_gemm": [(128, 7168, 16384), (128, 4096, 7168), (128, 7168, 2048)],
+    "ref_group": [
+        ([80, 176, 128, 72, 64, 248, 96, 160], [4096] * 8, [7168] * 8),
+        ([40, 76, 168, 72, 164, 148, 196, 160], [7168] * 8, [2048] * 8),
+        ([192, 320], [3072] * 2, [4096] * 2),
+        ([128, 384], [4096] * 2, [1536] * 2),
+    ],
+}
+REF_INSTALL = os.path.join(ROOT, "baseline", "_ref")
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--config", default="c4b", choices=sorted(WORKLOADS))
+    ap.add_argument("--config", default="c4b", choices=sorted(WORKLOADS) + sorted(COMPARE_SETS),
+                    help="a BASELINE.json config, or ref_gemm / ref_group: the reference's own "
+                         "benchmark shapes, timed beside torch._scaled_mm and the reference's CuTe "
+                         "kernels (one JSON line per shape)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", nargs="?", const="nccl", default=None, choices=["nccl", "p2p"],
                     help="c4b: every rank gets the whole C: nccl (default) = GEMM + NCCL all-gather; "
@@ -573,8 +590,155 @@ def bench_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- same-box comparison
+def _load_ref_module(task_dir, name):
+    """Import one module of the reference's task directory (they import ``task``, ``utils``
+    and ``reference`` by bare name, so those are swapped in for the import)."""
+    import importlib
+    for m in ("task", "utils", "reference", "submission"):
+        sys.modules.pop(m, None)
+    sys.path.insert(0, task_dir)
+    try:
+        return importlib.import_module(name)
+    finally:
+        sys.path.remove(task_dir)
+
+
+def _time_events(fn, runs, flush):
+    """Median ms of ``fn`` per call: CUDA events on the current stream around each call,
+    with the L2 flushed before it (as the reference's harness times, kernels/gemm/utils.py)."""
+    import torch
+    times = []
+    for _ in range(runs):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    return statistics.median(times)
+
+
+def _time_graph(fn, steps=20, reps=10):
+    """ms per call of ``fn`` replayed back to back from a CUDA graph (None if capture fails)."""
+    import torch
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(steps):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(reps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            g.replay()
+            e.record()
+            torch.cuda.synchronize()
+            t = s.elapsed_time(e) / steps
+            best = t if best is None else min(best, t)
+        return best
+    except Exception:
+        torch.cuda.synchronize()
+        return None
+
+
+def bench_compare(args):
+    """Ours vs torch._scaled_mm (the reference's ref_kernel arithmetic) vs the reference's own
+    CuTe DSL kernels (``submission.custom_kernel``) on the reference's benchmark shapes, on
+    inputs drawn by the reference's own ``generate_input``, each checked with the
+    reference's ``check_implementation``.  Needs the reference installed under baseline/_ref."""
+    import torch
+    from nvfp4_hackathon_b200 import _native, gemm, group_gemm
+    torch.cuda.set_device(0)
+    _native.load()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    family = "gemm" if args.config == "ref_gemm" else "group_gemm"
+    task_dir = os.path.join(REF_INSTALL, "kernels", family)
+    if not os.path.isdir(task_dir):
+        print(json.dumps({"config": args.config, "unavailable": f"{task_dir} missing (install the reference)"}))
+        return
+    ref = _load_ref_module(task_dir, "reference")
+    sub, sub_err = None, None
+    try:
+        sys.path.insert(0, task_dir)
+        sub = _load_ref_module(task_dir, "submission")
+    except Exception as ex:  # the CuTe DSL may not import on this box
+        sub_err = f"{type(ex).__name__}: {ex}"[:300]
+    finally:
+        if task_dir in sys.path:
+            sys.path.remove(task_dir)
+    hbm, bf16, _ = measured_peaks()
+    runs = max(10, min(args.steps, 50))
+    for case in COMPARE_SETS[args.config]:
+        if family == "gemm":
+            m, n, k = case
+            data = ref.generate_input(m=m, n=n, k=k, l=1, seed=1111)
+            flops, nbytes = dense_flops(m, n, k), dense_bytes(m, n, k)
+            ours = lambda: gemm.custom_kernel(data)
+            sa = ref.to_blocked(data[2][:, :, 0]).cuda()
+            sb = ref.to_blocked(data[3][:, :, 0]).cuda()
+            a0, bt = data[0][:, :, 0], data[1][:, :, 0].transpose(0, 1)
+            cublas = lambda: torch._scaled_mm(a0, bt, sa, sb, bias=None, out_dtype=torch.float16)
+            theirs = (lambda: sub.custom_kernel(data)) if sub else None
+            check = lambda out: ref.check_implementation(data, out)
+            shape = {"m": m, "n": n, "k": k}
+        else:
+            ms, ns, ks = case
+            data = ref.generate_input(m=ms, n=ns, k=ks, g=len(ms), seed=1111)
+            flops = sum(2.0 * a * b * c for a, b, c in zip(ms, ns, ks))
+            nbytes = sum(dense_bytes(a, b, c) for a, b, c in zip(ms, ns, ks))
+            ours = lambda: group_gemm.custom_kernel(data)
+            blocked = [(ref.to_blocked(sa[:, :, 0]).cuda(), ref.to_blocked(sb[:, :, 0]).cuda())
+                       for sa, sb in data[1]]
+
+            def cublas():
+                for (a, b, _), (sa, sb) in zip(data[0], blocked):
+                    torch._scaled_mm(a[:, :, 0], b[:, :, 0].transpose(0, 1), sa, sb, bias=None,
+                                     out_dtype=torch.float16)
+            theirs = (lambda: sub.custom_kernel(data)) if sub else None
+            check = lambda out: ref.check_implementation(data, out)
+            shape = {"m": ms, "n": ns, "k": ks}
+        line = {"config": args.config, "shape": shape, "flops": flops, "algorithmic_bytes": nbytes}
+        roof_us = max(flops / (4.0 * bf16 * 1e12), nbytes / (hbm * 1e9)) * 1e6
+        line["roofline_us"] = round(roof_us, 2)
+        for name, fn in (("ours", ours), ("scaled_mm", cublas), ("reference_cute", theirs)):
+            if fn is None:
+                line[name] = {"unavailable": sub_err}
+                continue
+            try:
+                out = fn()
+                torch.cuda.synchronize()
+                entry = {}
+                if name != "scaled_mm":
+                    ok, msg = check(out)
+                    entry["check_implementation"] = "pass" if ok else f"FAIL {str(msg)[:200]}"
+                for _ in range(3):
+                    fn()
+                ev = _time_events(fn, runs, flush)
+                entry["us_events_l2_flushed"] = round(ev * 1e3, 2)
+                gr = _time_graph(fn)
+                entry["us_graph"] = round(gr * 1e3, 2) if gr is not None else None
+                best = gr if gr is not None else ev
+                entry["tflops"] = round(flops / (best * 1e-3) / 1e12, 1)
+                entry["roofline_frac"] = round(roof_us / (best * 1e3), 3)
+                line[name] = entry
+            except Exception as ex:
+                torch.cuda.synchronize()
+                line[name] = {"error": f"{type(ex).__name__}: {ex}"[:300]}
+        if _native.status():
+            line["ours_device_status"] = _native.status()
+            _native.status_reset()
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.config in COMPARE_SETS:
+        bench_compare(args)
+        return
     if args.impl == "reference":
         bench_reference(args)
     else:

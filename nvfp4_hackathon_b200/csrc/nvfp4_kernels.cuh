@@ -741,7 +741,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
 #pragma unroll
         for (int c = 0; c < kPhase; ++c) {
           const int qc = q_lo + (c0 + c) * 32;
-          if (qc >= ti.q_rows) break;
+          if (c0 + c >= kChunks || qc >= ti.q_rows) break;
           if constexpr (!SWAP) {
             __half* dst = Cd + (long long)p * ti.ldc + qc;
             if (qc + 32 <= ti.q_rows && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
@@ -914,7 +914,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
 #pragma unroll
         for (int cc = 0; cc < kPhase; ++cc) {
           const int c = c0 + cc;
-          if (q_lo + c * 32 < ti.q_rows) {  // warp-uniform
+          if (c < kChunks && q_lo + c * 32 < ti.q_rows) {  // warp-uniform (BN = 192: 3 chunks)
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
               uint32_t r[16];

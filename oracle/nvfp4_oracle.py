@@ -23,9 +23,11 @@ Number formats (the torch dtypes the reference uses):
   subnormals for exponent 0, 0x7F / 0xFF = NaN, no infinities.
 
 Parity pin: the layout functions are checked against fixtures produced by the
-reference's own ``to_blocked`` (tests/golden/make_golden.py), and the GEMM
-semantics against ``torch._scaled_mm`` (the reference's ``ref_kernel`` call) on
-the GPU box (tests/test_gpu_parity.py::test_oracle_matches_scaled_mm).
+reference's own ``to_blocked`` (tests/golden/make_layout_golden.py); the GEMM
+semantics against ``torch._scaled_mm`` outputs (tests/golden/make_scaled_mm_golden.py,
+and live on the GPU in tests/test_gpu_parity.py::test_oracle_matches_scaled_mm), and
+against the reference's own ``generate_input`` + ``ref_kernel`` run on a B200
+(tests/golden/make_reference_fixtures.py).
 """
 from __future__ import annotations
 

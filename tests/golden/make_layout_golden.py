@@ -1,6 +1,7 @@
 """Generate tests/golden/to_blocked_golden.npz from the reference's own code.
 
-Run in a checkout that has the reference at REF (default /root/reference); it
+Run with REF, the root of a checkout of the reference (the directory holding
+``kernels/``), as the argument or in the NVFP4_REF_ROOT environment variable; it
 imports ``to_blocked`` from kernels/gemm/reference.py and
 kernels/group_gemm/reference.py (pure torch, runs on the CPU) and records its
 outputs on seeded random scale matrices, plus torch's float8_e4m3fn decode of
@@ -33,7 +34,9 @@ def load(path, name):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NVFP4_REF_ROOT")
+    if not ref:
+        sys.exit("usage: make_layout_golden.py REF (or set NVFP4_REF_ROOT)")
     gemm_ref = load(os.path.join(ref, "kernels/gemm/reference.py"), "ref_gemm_reference")
     group_ref = load(os.path.join(ref, "kernels/group_gemm/reference.py"), "ref_group_reference")
     rng = np.random.default_rng(2024)

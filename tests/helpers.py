@@ -31,3 +31,14 @@ def dense_expected(data, rows=None, dtype=None) -> np.ndarray:
 def assert_close(got: np.ndarray, exp: np.ndarray, what=""):
     bad = orc.allclose_report(got, exp, rtol=RTOL, atol=ATOL)
     assert not bad, f"{what}: " + " ".join(bad)
+
+
+def spread_rows(m: int, block: int = 128, salt: int = 37) -> np.ndarray:
+    """One row in every ``block``-row block of M at a varying offset, plus the first and
+    last rows: a sample that touches every M-tile row block of the kernel's raster."""
+    nb = (m + block - 1) // block
+    rows = {0, m - 1}
+    for b in range(nb):
+        r = b * block + (b * salt + 11) % block
+        rows.add(min(m - 1, r))
+    return np.array(sorted(rows), dtype=np.int64)

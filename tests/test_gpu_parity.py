@@ -8,7 +8,7 @@ import torch
 
 from nvfp4_hackathon_b200 import _native, gemm, group_gemm, inputs
 from oracle import nvfp4_oracle as orc
-from tests.helpers import assert_close, dense_expected, u8
+from tests.helpers import assert_close, dense_expected, spread_rows, u8
 
 pytestmark = pytest.mark.gpu
 
@@ -46,7 +46,7 @@ def test_baseline_8192_cubed_sampled_rows(cuda):
     m = n = k = 8192
     data = inputs.generate_quantized_input(m, n, k, 1, seed=1111)
     got = _run_dense(data)
-    rows = np.r_[0:64, 4000:4064, 8128:8192]
+    rows = spread_rows(m)  # one row in every 128-row M block
     exp = dense_expected(data, rows=rows, dtype=np.float32)
     assert_close(got[:, rows], exp, "8192^3 sampled rows")
 
@@ -201,9 +201,14 @@ def test_grouped_config4a_sampled(cuda):
     ms = inputs.zipf_group_sizes(64, 32768)
     gdata = inputs.generate_quantized_group_input(ms, 2048, 7168, seed=1111)
     got = _run_grouped(gdata)
-    exp = _grouped_expected(gdata, rows=48)
-    for g, (x, e) in enumerate(zip(got, exp)):
-        assert_close(x[:48], e, f"c4a group {g}")
+    for g, ((a, b, _), (sa, sb)) in enumerate(zip(gdata[0], gdata[1])):
+        if ms[g] == 0:
+            continue
+        rows = spread_rows(ms[g], block=128)
+        e = orc.grouped_gemm_ref([(u8(a[:, :, 0])[rows], u8(b[:, :, 0]),
+                                   u8(sa[:, :, 0].contiguous())[rows],
+                                   u8(sb[:, :, 0].contiguous()))], dtype=np.float32)[0]
+        assert_close(got[g][rows], e, f"c4a group {g}")
 
 
 def test_grouped_empty_groups_and_reuse(cuda):

@@ -6,15 +6,16 @@ fails, a run that stops at the first failure has already run everything else.
 
 The test calls the entry point through the C ABI twice in a row, on two
 different problems, and compares each result with the ordinary entry point
-(which uses a caller-provided workspace), with the tolerance of the other
-parity tests.
+(which uses a caller-provided workspace) and with the CPU oracle, with the
+tolerance of the other parity tests.
 """
 import numpy as np
 import pytest
 import torch
 
 from nvfp4_hackathon_b200 import _native, group_gemm, inputs
-from tests.helpers import assert_close
+from oracle import nvfp4_oracle as orc
+from tests.helpers import assert_close, u8
 
 pytestmark = pytest.mark.gpu
 
@@ -49,8 +50,12 @@ def test_noalloc_matches_workspace_entry_point_two_calls(cuda, first):
         _native.check(rc, "nvfp4_grouped_gemm_noalloc")
         torch.cuda.synchronize()
         _native.raise_on_device_error()
-        for g, ((_, _, c), e) in enumerate(zip(g2[0], expected)):
-            assert_close(c[:, :, 0].cpu().numpy(), e, f"call {i} group {g}")
+        for g, ((a, b, c), (sa, sb), e) in enumerate(zip(g2[0], g2[1], expected)):
+            got = c[:, :, 0].cpu().numpy()
+            assert_close(got, e, f"call {i} group {g} vs workspace entry point")
+            ref = orc.grouped_gemm_ref([(u8(a[:, :, 0].contiguous()), u8(b[:, :, 0].contiguous()),
+                                         u8(sa[:, :, 0].contiguous()), u8(sb[:, :, 0].contiguous()))])[0]
+            assert_close(got, ref, f"call {i} group {g} vs oracle")
 
 
 def test_noalloc_rejects_too_many_groups(cuda):

@@ -94,14 +94,17 @@ def dist_env():
     return rank, world, local
 
 
-def measured_peaks():
+def measured_peaks(sustained=False):
+    """(HBM GB/s, bf16 TFLOP/s, source): the pool's measured copy bandwidth and cuBLAS bf16
+    rate, burst or (sustained=True) the seconds-long rate under the power cap."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+        bf16 = float(d["bf16_tflops_sustained"] if sustained else d["bf16_tflops"])
+        return float(d["hbm_gbs"]), bf16, "measured"
     except Exception:
-        return 6650.0, 1590.0, "fallback"
+        return 6650.0, 1400.0 if sustained else 1590.0, "fallback"
 
 
 def profile_traffic(kernel_tag: str):
@@ -411,32 +414,56 @@ def bench_ours(args):
         del gathered
 
     # ---------------------------------------------------------------- e2e (host buffers)
+    # Every step copies its inputs from pinned host memory, runs the GEMM through the public
+    # entry point and copies C back to pinned host memory.  Two device buffer sets and three
+    # streams pipeline the steps: step i's host->device copy, step i-1's GEMM and step i-2's
+    # device->host copy run at the same time (PCIe carries both directions at once).
     e2e_steps = args.e2e_steps or min(args.steps, 50)
-    dev_in = _step_inputs(wl)
+    sets = [wl, copies[1] if n_copies > 1 else Workload(args.config, rank, world, device,
+                                                        gather=args.gather, copy=1)]
+    dev_in = [_step_inputs(w) for w in sets]
+    outs = [_step_outputs(w) for w in sets]
     host_in = []
-    for d in dev_in:
+    for d in dev_in[0]:
         h = torch.empty(d.numel(), dtype=torch.uint8, pin_memory=True)
         h.copy_(d.cpu())
         host_in.append(h)
-    outs = _step_outputs(wl)
-    host_out = [torch.empty(o.numel(), dtype=torch.uint8, pin_memory=True) for o in outs]
+    host_out = [[torch.empty(o.numel(), dtype=torch.uint8, pin_memory=True) for o in oo] for oo in outs]
     h2d = sum(h.numel() for h in host_in)
-    d2h = sum(h.numel() for h in host_out)
+    d2h = sum(h.numel() for h in host_out[0])
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev = lambda: torch.cuda.Event()
+    ev_in, ev_run, ev_out = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+    for b in range(2):  # all buffers start free
+        ev_run[b].record(stream)
+        ev_out[b].record(stream)
 
-    def e2e_step():
-        for h, d in zip(host_in, dev_in):
-            d.copy_(h, non_blocking=True)
-        wl.run()
-        for h, o in zip(host_out, outs):
-            h.copy_(o, non_blocking=True)
+    def e2e_step(i):
+        b = i & 1
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_run[b])  # the GEMM that last read these inputs is done
+            for h, d in zip(host_in, dev_in[b]):
+                d.copy_(h, non_blocking=True)
+            ev_in[b].record(s_in)
+        stream.wait_event(ev_in[b])
+        stream.wait_event(ev_out[b])  # C of this buffer set has been copied out
+        sets[b].run()
+        ev_run[b].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_run[b])
+            for h, o in zip(host_out[b], outs[b]):
+                h.copy_(o, non_blocking=True)
+            ev_out[b].record(s_out)
 
-    for _ in range(3):
-        e2e_step()
+    for i in range(4):
+        e2e_step(i)
     barrier()
     es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     es.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    stream.wait_event(ev_out[0])
+    stream.wait_event(ev_out[1])
     ee.record(stream)
     barrier()
     t_wall1 = time.time()
@@ -460,11 +487,16 @@ def bench_ours(args):
                     "frac": round(achieved / hbm_peak, 4),
                     "peak_source": f"{peak_src} hbm_gbs (burst copy), kernel timed alone"}
         else:
-            fp4_peak = 4.0 * bf16_peak
+            # the timed region is >= 1 s of back-to-back launches, so the denominator is the
+            # sustained rate under the 1 kW power cap (the burst one is reported beside it)
+            _, bf16_sus, _ = measured_peaks(sustained=True)
+            fp4_peak = 4.0 * bf16_sus
             achieved = wl.flops / avg_s / 1e12
             roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(fp4_peak, 1),
                     "unit": "TFLOP/s", "frac": round(achieved / fp4_peak, 4),
-                    "peak_source": f"4 x {peak_src} bf16_tflops (dense fp4 rate = 4x bf16 on B200)"}
+                    "frac_of_burst_peak": round(achieved / (4.0 * bf16_peak), 4),
+                    "peak_source": f"4 x {peak_src} bf16_tflops_sustained (dense fp4 rate = 4x bf16 "
+                                   f"on B200; kernel timed inside >= 1 s of back-to-back launches)"}
         tag = "nvfp4_gemm_" if wl.kind.startswith("dense") else "nvfp4_grouped_"
         roof["traffic"] = profile_traffic(tag + args.config)
         roof["algorithmic_bytes_per_launch"] = wl.bytes
@@ -486,7 +518,9 @@ def bench_ours(args):
             "roofline": roof,
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                    "path": "pinned host -> device copies, custom_kernel, device -> host copy"},
+                    "path": "pinned host -> device copies, custom_kernel, device -> host copy of C, "
+                            "every step; two buffer sets on three streams overlap step i's upload, "
+                            "step i-1's GEMM and step i-2's download"},
             "gpu_launches": wl.launches_per_step * (args.steps * reps + e2e_steps),
             "clocks": sampler.summary(t_wall0, t_wall1),
         }

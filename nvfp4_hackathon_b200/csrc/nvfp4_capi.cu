@@ -131,6 +131,26 @@ int encode_sf_map(CUtensorMap* m, const void* ptr, long long mn, long long k, lo
   return NVFP4_OK;
 }
 
+// Store map of C (fp16 / bf16, (L, M, N) row-major, row stride N) for the TMA epilogue: the
+// box is 16 columns x 32 rows (32-byte rows, 32-byte swizzle), or for the swapped operand
+// order 32 columns x 16 rows (64-byte rows, 64-byte swizzle).  Needs N % 8 == 0 and a
+// 16-byte aligned C (TMA strides and base).
+int encode_c_map(CUtensorMap* m, const void* ptr, long long rows, long long cols, long long batch,
+                 bool swap) {
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(cols * 2), (cuuint64_t)(rows * cols * 2)};
+  cuuint32_t box[3] = {swap ? 32u : 16u, swap ? 16u : 32u, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(ptr), dims, strides,
+                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swap ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(NVFP4_ERR_DRIVER, "cuTensorMapEncodeTiled (C) failed (%d) rows=%lld cols=%lld", (int)r,
+                rows, cols);
+  return NVFP4_OK;
+}
+
 // Per-thread memo of recent operand maps: a repeated call on the same buffers skips
 // the driver encode (about a microsecond each).  The key covers every input of the
 // encoding, so a hit is exactly the map the driver would build again.
@@ -138,7 +158,7 @@ struct MapKey {
   const void* ptr;
   long long rows, kbytes, batch;
   int box_rows, box_inner;
-  int kind;  // 0 operand map, 1 scale-factor map
+  int kind;  // 0 operand map, 1 scale-factor map, 2 C store map
   bool operator==(const MapKey& o) const {
     return ptr == o.ptr && rows == o.rows && kbytes == o.kbytes && batch == o.batch &&
            box_rows == o.box_rows && box_inner == o.box_inner && kind == o.kind;
@@ -161,9 +181,11 @@ int cached_map(CUtensorMap* m, int kind, const void* ptr, long long rows, long l
       *m = g_map_cache[i].map;
       return NVFP4_OK;
     }
-  // (scale maps: rows = mn, kbytes = k, box_rows = blocks, box_inner = KB)
-  int rc = kind == 0 ? encode_operand_map(m, ptr, rows, kbytes, batch, box_rows, box_inner)
-                     : encode_sf_map(m, ptr, rows, kbytes, batch, box_inner, box_rows);
+  // (scale maps: rows = mn, kbytes = k, box_rows = blocks, box_inner = KB;
+  //  C maps: rows = m, kbytes = n, box_inner = operand order swapped)
+  int rc = kind == 0   ? encode_operand_map(m, ptr, rows, kbytes, batch, box_rows, box_inner)
+           : kind == 1 ? encode_sf_map(m, ptr, rows, kbytes, batch, box_inner, box_rows)
+                       : encode_c_map(m, ptr, rows, kbytes, batch, box_inner != 0);
   if (rc) return rc;
   MapEntry& e = g_map_cache[g_map_next];
   g_map_next = (g_map_next + 1) % kMapCache;
@@ -212,7 +234,7 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 
 template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false, bool SK = false, bool F32 = false>
 int launch(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tsp,
-           const CUtensorMap& tsq, const GemmParams& prm, int grid,
+           const CUtensorMap& tsq, const CUtensorMap& tc, const GemmParams& prm, int grid,
            cudaStream_t stream) {
   using C_ = Cfg<BN, KB, CTA2>;
   auto kern = nvfp4_gemm_kernel<GROUPED, SWAP, BN, KB, CTA2, SK, F32>;
@@ -228,7 +250,7 @@ int launch(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tsp,
     attr_done[dev].store(true, std::memory_order_release);
   }
   cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kNumThreads), smem, stream,
-                             CTA2 ? 2 : 1, SK, tp, tq, tsp, tsq, prm);
+                             CTA2 ? 2 : 1, SK, tp, tq, tsp, tsq, tc, prm);
   if (e != cudaSuccess) return cuda_fail(e, "nvfp4_gemm_kernel launch");
   return NVFP4_OK;
 }
@@ -243,8 +265,11 @@ struct DenseChoice {
 DenseChoice choose_dense(int m, int n, int k, const nvfp4_options* opt) {
   (void)k;
   DenseChoice c;
+  // M >= 256 with a wide N: M = 256 x N = 256 tiles on a CTA pair (each SM stages 128 rows of
+  // A and 128 of B per k-step instead of 128 + 256: a third fewer bytes per MMA cycle).
   if (m <= 64) c = {true, 64, 4, false};
   else if (m <= 128) c = {true, 128, 4, false};
+  else if (m >= 256 && n >= 2048 && !(opt && opt->out_dtype == 2)) c = {false, 256, 4, true};
   else c = {false, (n >= 2048) ? 256 : 128, 4, false};
   if (opt) {
     if (opt->cta_pair == 1) c.cta2 = false;
@@ -333,6 +358,13 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   if (rc) return rc;
   rc = cached_map(&tsq, 1, sfQ, q_rows, k, l, Cfg<BN, KB, CTA2>::kSfqAtoms, KB);
   if (rc) return rc;
+  // TMA-store epilogue: one fp16/bf16 output buffer with 16-byte rows strides
+  const bool c_tma = !g_multi_out && !(opt && opt->out_dtype == 2) && n % 8 == 0 && aligned16(c);
+  CUtensorMap tc = tp;  // (unused unless c_tma)
+  if (c_tma) {
+    rc = cached_map(&tc, 2, c, m, n, l, 0, SWAP ? 1 : 0);
+    if (rc) return rc;
+  }
   GemmParams prm;
   std::memset(&prm, 0, sizeof(prm));
   prm.p_rows = p_rows;
@@ -360,6 +392,7 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   if (total > 0x7fffffffLL) return fail(NVFP4_ERR_UNSUPPORTED, "too many tiles");
   prm.total_tiles = (int)total;
   prm.q_fastest = 0;
+  prm.c_tma = c_tma ? 1 : 0;
   prm.status = (opt && opt->dev_status) ? opt->dev_status : st->status;
   prm.timeout_ns = (opt && opt->timeout_ns) ? opt->timeout_ns : g_timeout_ns.load();
   prm.debug = opt ? (opt->debug & 1) : 0;
@@ -402,7 +435,7 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
       prm.sk_ktn = ktn;
       prm.sk_flags = static_cast<unsigned*>(ws);
       prm.sk_slots = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kSkMaxCtas * sizeof(unsigned));
-      rc = launch<false, SWAP, BN, KB, CTA2, true>(tp, tq, tsp, tsq, prm, g, stream);
+      rc = launch<false, SWAP, BN, KB, CTA2, true>(tp, tq, tsp, tsq, tc, prm, g, stream);
       if (rc == NVFP4_OK) return rc;
       // (a cooperative launch the device refuses: run the plain schedule instead)
       cudaGetLastError();
@@ -411,9 +444,9 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   }
   if (opt && opt->out_dtype == 2) {
     if constexpr (CTA2) return fail(NVFP4_ERR_UNSUPPORTED, "fp32 C is not built for CTA pairs");
-    else return launch<false, SWAP, BN, KB, false, false, true>(tp, tq, tsp, tsq, prm, grid, stream);
+    else return launch<false, SWAP, BN, KB, false, false, true>(tp, tq, tsp, tsq, tc, prm, grid, stream);
   }
-  return launch<false, SWAP, BN, KB, CTA2>(tp, tq, tsp, tsq, prm, grid, stream);
+  return launch<false, SWAP, BN, KB, CTA2>(tp, tq, tsp, tsq, tc, prm, grid, stream);
 }
 
 // ------------------------------------------------------------------ grouped GEMM
@@ -426,7 +459,7 @@ constexpr int kGroupedBN = 256;
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 size_t grouped_ws_bytes(int G) {
-  return align_up((size_t)G * 2 * sizeof(CUtensorMap), 256) + align_up((size_t)(G + 1) * 4, 256);
+  return align_up((size_t)G * 3 * sizeof(CUtensorMap), 256) + align_up((size_t)(G + 1) * 4, 256);
 }
 
 __device__ __forceinline__ void tmap_replace_addr(void* m, const void* p) {
@@ -450,14 +483,15 @@ __device__ __forceinline__ void tmap_replace_stride(void* m, uint64_t v) {
                : "memory");
 }
 
-// One thread per group: validate the group, clone the two template maps into
-// the workspace and point them at the group's B (P side) and A (Q side), then
-// a block-wide scan turns per-group tile counts into the schedule prefix.
+// One thread per group: validate the group, clone the three template maps into
+// the workspace and point them at the group's B (P side), A (Q side) and C (the TMA
+// store map, when n % 8 == 0 and C is 16-byte aligned), then a block-wide scan turns
+// per-group tile counts into the schedule prefix.
 __global__ void __launch_bounds__(kMaxGroups)
 nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_constant__ CUtensorMap tmpl_q,
-                   const int* __restrict__ sizes, const unsigned long long* __restrict__ abc,
+                   const __grid_constant__ CUtensorMap tmpl_c, const int* __restrict__ sizes, const unsigned long long* __restrict__ abc,
                    const unsigned long long* __restrict__ sfs, int G, CUtensorMap* maps,
-                   int* prefix, int bn, int* status) {
+                   int* prefix, int pm, int bn, int* status) {
   __shared__ int warp_sums[kMaxGroups / 32];
   pdl_launch_dependents();
   // the workspace may still be read by the previous call's GEMM on this stream
@@ -475,9 +509,9 @@ nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_cons
     if (!valid) {
       atomicCAS(status, 0, 5 /* NVFP4_STATUS_BAD_GROUP */);
     } else if (!empty) {
-      tiles = ((n + kBM - 1) / kBM) * ((m + bn - 1) / bn);
-      CUtensorMap* mp = maps + 2 * g;
-      CUtensorMap* mq = maps + 2 * g + 1;
+      tiles = ((n + pm - 1) / pm) * ((m + bn - 1) / bn);  // (pm = 256 for CTA pairs)
+      CUtensorMap* mp = maps + 3 * g;
+      CUtensorMap* mq = maps + 3 * g + 1;
       *mp = tmpl_p;
       *mq = tmpl_q;
       const uint64_t kbytes = (uint64_t)k / 2;
@@ -491,6 +525,15 @@ nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_cons
       tmap_replace_dim<1>(mq, (uint32_t)m);
       tmap_replace_stride<0>(mq, kbytes);
       tmap_replace_stride<1>(mq, kbytes * (uint64_t)m);
+      if ((n & 7) == 0 && (pc & 15ull) == 0) {
+        CUtensorMap* mc = maps + 3 * g + 2;
+        *mc = tmpl_c;
+        tmap_replace_addr(mc, reinterpret_cast<const void*>(pc));
+        tmap_replace_dim<0>(mc, (uint32_t)n);
+        tmap_replace_dim<1>(mc, (uint32_t)m);
+        tmap_replace_stride<0>(mc, 2ull * (uint64_t)n);
+        tmap_replace_stride<1>(mc, 2ull * (uint64_t)n * (uint64_t)m);
+      }
       asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
     }
   }
@@ -520,7 +563,7 @@ nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_cons
   if (g == 0) prefix[0] = 0;
 }
 
-template <int BN, int KB = 4>
+template <int BN, int KB = 4, bool CTA2 = false>
 int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sfs, int G, void* ws,
                    cudaStream_t stream, DeviceState* st, const nvfp4_options* opt) {
   // Templates: any valid 16-byte-aligned address and sizes; the prep kernel
@@ -528,15 +571,19 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   CUtensorMap tp, tq;
   int rc = encode_operand_map(&tp, ws, 128, 128, 1, kBM, KB * 32);
   if (rc) return rc;
-  rc = encode_operand_map(&tq, ws, 128, 128, 1, BN, KB * 32);
+  rc = encode_operand_map(&tq, ws, 128, 128, 1, CTA2 ? BN / 2 : BN, KB * 32);
+  if (rc) return rc;
+  CUtensorMap tc;
+  rc = encode_c_map(&tc, ws, 64, 64, 1, /*swap=*/true);
   if (rc) return rc;
   CUtensorMap* maps = static_cast<CUtensorMap*>(ws);
   int* prefix = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) +
-                                       align_up((size_t)G * 2 * sizeof(CUtensorMap), 256));
+                                       align_up((size_t)G * 3 * sizeof(CUtensorMap), 256));
   const int threads = ((G + 31) / 32) * 32;
-  cudaError_t e = launch_pdl(nvfp4_grouped_prep, dim3(1), dim3(threads), 0, stream, 1, false, tp, tq, sizes,
+  cudaError_t e = launch_pdl(nvfp4_grouped_prep, dim3(1), dim3(threads), 0, stream, 1, false, tp, tq, tc, sizes,
                              reinterpret_cast<const unsigned long long*>(abc),
-                             reinterpret_cast<const unsigned long long*>(sfs), G, maps, prefix, BN,
+                             reinterpret_cast<const unsigned long long*>(sfs), G, maps, prefix,
+                             CTA2 ? 2 * kBM : kBM, BN,
                              (opt && opt->dev_status) ? opt->dev_status : st->status);
   if (e != cudaSuccess) return cuda_fail(e, "nvfp4_grouped_prep launch");
   GemmParams prm;
@@ -552,8 +599,10 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   prm.debug = opt ? (opt->debug & 1) : 0;
   int grid = st->num_sms;
   if (opt && opt->max_ctas > 0 && opt->max_ctas < grid) grid = opt->max_ctas;
-  // (the grouped kernel copies scales with plain bulk copies: the scale maps are unused)
-  return launch<true, true, BN, KB>(tp, tq, tp, tq, prm, grid, stream);
+  if (CTA2) grid = grid / 2 < 1 ? 2 : grid / 2 * 2;  // whole pairs
+  // (the grouped kernel copies scales with plain bulk copies: the scale maps are unused, and
+  // its operand and C maps are the per-group ones in the workspace)
+  return launch<true, true, BN, KB, CTA2>(tp, tq, tp, tq, tc, prm, grid, stream);
 }
 
 }  // namespace
@@ -735,6 +784,11 @@ int nvfp4_grouped_gemm_ex(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int bn = (opt && opt->tile_n > 0) ? opt->tile_n : kGroupedBN;
+  if (opt && opt->cta_pair == 2) {  // 256 rows of B_g per tile on a CTA pair
+    if (bn == 128) return run_grouped_bn<128, 4, true>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
+    if (bn == 256) return run_grouped_bn<256, 4, true>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
+    return fail(NVFP4_ERR_UNSUPPORTED, "grouped CTA pairs are built for tile_n 128 and 256 (got %d)", bn);
+  }
   switch (bn) {
     case 64: return run_grouped_bn<64>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
     case 128:
@@ -785,13 +839,13 @@ int nvfp4_quantize(const void* x, int dtype, int rows, int k, int l, void* codes
 
 // ------------------------------------------------------------------ grouped GEMM without allocation
 // Scratch for nvfp4_grouped_gemm_noalloc: room for the per-group tensor maps and
-// the tile prefix of up to kNoAllocMaxGroups groups (about 66 KiB).  Every GPU
+// the tile prefix of up to kNoAllocMaxGroups groups (about 97 KiB).  Every GPU
 // that loads the library holds one copy until the process exits.  In host code
 // the name below is only a host-side stand-in; the device address comes from
 // cudaGetSymbolAddress, once per device.
 constexpr int kNoAllocMaxGroups = 256;
 constexpr size_t kNoAllocScratchBytes =
-    ((size_t)kNoAllocMaxGroups * 2 * sizeof(CUtensorMap) + 255) / 256 * 256 +
+    ((size_t)kNoAllocMaxGroups * 3 * sizeof(CUtensorMap) + 255) / 256 * 256 +
     ((size_t)(kNoAllocMaxGroups + 1) * 4 + 255) / 256 * 256;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

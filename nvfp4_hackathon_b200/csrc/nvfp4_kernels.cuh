@@ -14,20 +14,21 @@
 //
 // Roles (20 warps):
 //   warps 0-7   epilogue: warp w drains TMEM lanes 32*(w%4).. and column half w/4 of the
-//               accumulator into registers as fp16, releases the accumulator, then stores
-//               to global while the next tile's MMAs already run
+//               accumulator into registers as fp16 (two 32-column chunks at a time),
+//               releases the accumulator after its last load, and stores C with TMA through
+//               small shared-memory staging buffers while the next tile's MMAs already run
 //   warps 8-10  producers (k-steps round-robin): TMA loads of the P and Q tiles (128-byte
-//               swizzle) into a ring of kStages stages, and the scale atoms (dense: tensor
-//               loads through 8-byte-element scale maps; grouped: plain bulk copies) into
-//               their own ring of slots, kSfLead k-steps ahead of the operands
+//               swizzle) into a ring of kStages stages
 //   warp 11     TMEM owner and MMA issuer: per k-step it waits for the stage's operand
-//               tiles (full) and scales (sf_full), issues tcgen05.mma kind::mxf4nvf4
-//               (K = 64 per instruction) and one tcgen05.commit to release the stage.
+//               tiles (full) and its scales in TMEM (sf_full), issues tcgen05.mma
+//               kind::mxf4nvf4 (K = 64 per instruction) and two tcgen05.commits (the stage,
+//               the TMEM scale buffer)
 //   warps 12-19 scale warps, two groups of four (group g serves k-steps j with j % 2 == g):
-//               each warp moves the step's scale atoms from their slot into its own 32
-//               TMEM lanes with ld.shared + tcgen05.st, once the step's TMEM scale buffer
-//               is free (the stage's previous MMAs committed).  tcgen05.cp would run in
-//               the MMA's own queue (~56 cycles per 512-byte atom, not overlapped with the
+//               the group loads its steps' scale atoms into its own shared-memory slots
+//               (dense: tensor loads through 8-byte-element scale maps; grouped: plain bulk
+//               copies), and each warp moves them into its own 32 TMEM lanes with ld.shared +
+//               tcgen05.st once the step's TMEM scale buffer is free.  tcgen05.cp would run
+//               in the MMA's own queue (~56 cycles per 512-byte atom, not overlapped with the
 //               MMAs), register stores run alongside them.
 //   CTA pairs (cta_group::2, M = 256): the leader issues the MMAs; both CTAs' tensor loads
 //   count on the leader's full barrier and both CTAs' scale warps arrive on its sf_full.
@@ -62,7 +63,6 @@ constexpr int kFirstSfWarp = kMmaWarp + 1;
 constexpr int kSfGroups = 2;        // groups of 4 scale warps; group g serves k-steps j % 2 == g
 constexpr int kNumThreads = 32 * (kFirstSfWarp + 4 * kSfGroups);
 constexpr int kMaxDynamicSmem = 232448;     // opt-in dynamic shared memory per CTA on sm_100
-constexpr int kSmemBudget = kMaxDynamicSmem - 2560;  // minus alignment and barriers
 
 // KB = 64-wide K blocks per pipeline stage: 4 (256 K, one 128-byte swizzle row per
 // operand row) or 2 (128 K, 64-byte swizzle).  Smaller stages fit twice as many in
@@ -88,35 +88,48 @@ struct Cfg {
   static constexpr int kSfpCols = 4 * KB;
   static constexpr int kSfCols = kSfpCols + KB * kSfqColsPerKb;
   static constexpr int kAccStages = (BN <= 128) ? 2 : 1;
-  // one TMEM scale buffer per stage
-  static constexpr int kStagesSmem = kSmemBudget / (kStageBytes + kSfSlotBytes);
-  static constexpr int kStagesTmem = (512 - kAccStages * BN) / kSfCols;
-  static constexpr int kStagesRaw = kStagesSmem < kStagesTmem ? kStagesSmem : kStagesTmem;
-  static constexpr int kStagesCap = kStagesRaw > 8 ? 8 : kStagesRaw;
-  static constexpr int kStages = kStagesCap;
-  // Scale atoms travel in their own ring of shared-memory slots, loaded kSfLead k-steps
-  // ahead of the step's operand tiles, so the scale warps can move them into TMEM while
-  // the operands are still in flight.  Slot of step j is reused by step j + kSfSlots,
-  // loaded when the producer issues step j + kStages: the MMAs of step j have finished.
-  static constexpr int kSfLeadRaw =
-      (kSmemBudget - kStages * (kStageBytes + kSfSlotBytes)) / kSfSlotBytes;
-  static constexpr int kSfLead = kSfLeadRaw < kStages ? kSfLeadRaw : kStages;
-  static constexpr int kSfSlots = kStages + kSfLead;
-  static constexpr int kColsNeeded = kAccStages * BN + kStages * kSfCols;
+  // TMEM scale buffers: a ring of its own (kSfBufs deep), next to the accumulators.  The
+  // scales of step j go into buffer j % kSfBufs once the MMAs of step j - kSfBufs are done.
+  static constexpr int kSfBufsRaw = (512 - kAccStages * BN) / kSfCols;
+  static constexpr int kSfBufs = kSfBufsRaw > 8 ? 8 : kSfBufsRaw;
+  // Shared memory: [operand stages][epilogue staging][scale slots][barriers].
+  //
+  // Scale atoms travel in their own ring of NS shared-memory slots (even: slot j % NS is
+  // always served by the scale-warp group of step j, which loads it itself).  Operand stages
+  // first, as many as fit beside kMinSlots slots and 8 KB of epilogue staging (cap 8); then
+  // up to 8 slots in what is left.
+  static constexpr int kMinSlots = 4;
+  static constexpr int kAvail = kMaxDynamicSmem - 1024 /* base alignment */ - 512 /* barriers */;
+  static constexpr int kStagesRaw = (kAvail - kMinSlots * kSfSlotBytes - 8192) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static constexpr int kSfSlotsRaw = (kAvail - kStages * kStageBytes - 8192) / kSfSlotBytes;
+  static constexpr int kSfSlots = kSfSlotsRaw >= 8 ? 8 : (kSfSlotsRaw & ~1);
+  // Epilogue staging for the TMA stores of C: per epilogue warp kEpiBufs buffers of 1 KB
+  // (32 rows x 16 fp16 columns of C; 16 rows x 32 columns in the swapped order), two
+  // (double buffering) where they fit.
+  static constexpr int kRest = kAvail - kStages * kStageBytes - kSfSlots * kSfSlotBytes;
+  static constexpr int kEpiBufs = kRest >= 2 * kEpiWarps * 1024 ? 2 : 1;
+  static constexpr int kEpiBytes = kEpiBufs * kEpiWarps * 1024;
+  static constexpr int kColsNeeded = kAccStages * BN + kSfBufs * kSfCols;
   static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64
                                  : kColsNeeded <= 128 ? 128 : kColsNeeded <= 256 ? 256 : 512;
   static constexpr int kSfCol0 = kAccStages * BN;
-  // barriers: full[S], sf_full[S], empty[S], acc_full[A], acc_empty[A], drain, sf_data[slots]
-  static constexpr int kNumBars = 3 * kStages + 2 * kAccStages + 1 + kSfSlots;
+  // barriers: full[S], empty[S], sf_full[T], sf_empty[T], acc_full[A], acc_empty[A], drain,
+  // sf_data[NS], sf_free[NS]
+  static constexpr int kNumBars = 2 * kStages + 2 * kSfBufs + 2 * kAccStages + 1 + 2 * kSfSlots;
   static constexpr int kBarrierBytes = 8 * kNumBars + 16;
   static constexpr int kSmemBytes =
-      1024 + kStages * kStageBytes + kSfSlots * kSfSlotBytes + kBarrierBytes;
+      1024 + kStages * kStageBytes + kEpiBytes + kSfSlots * kSfSlotBytes + kBarrierBytes;
   // a producer's previous step j - kNumProducers must imply that step j - 2 S was consumed,
   // or its parity wait on the empty barrier for step j - S could alias
   static_assert(kStages >= kNumProducers, "need at least one stage per producer warp");
+  static_assert(kSfBufs >= 2, "TMEM scale ring too shallow");
+  static_assert(kSfSlots % kSfGroups == 0 && kSfSlots >= 2 * kSfGroups,
+                "each scale slot must belong to one scale-warp group");
   static_assert(kColsNeeded <= 512, "TMEM budget exceeded");
-  static_assert(kSfSlots <= 32, "slot bookkeeping uses 32-bit masks");
-  static_assert(kSmemBytes + 1024 <= kMaxDynamicSmem, "shared memory budget exceeded");
+  static_assert(kBarrierBytes <= 512, "barrier area exceeded");
+  static_assert(kSmemBytes <= kMaxDynamicSmem, "shared memory budget exceeded");
+  static_assert((kStages * kStageBytes) % 1024 == 0, "staging buffers must stay 1 KB aligned");
 };
 
 // Everything the kernel needs; tensor maps for the dense case are separate
@@ -138,7 +151,7 @@ struct GemmParams {
   const int* sizes;             // G x 4: m, n, k, l
   const unsigned long long* abc;  // G x 3: a, b, c
   const unsigned long long* sfs;  // G x 2: sfa (permuted), sfb (permuted)
-  const CUtensorMap* maps;      // G x 2: [P map = B_g, Q map = A_g]
+  const CUtensorMap* maps;      // G x 3: [P map = B_g, Q map = A_g, C_g store map]
   const int* tile_prefix;       // G + 1 running tile counts
   // stream-K (dense only): when sk_ktn > 0 every CTA takes an equal contiguous range of
   // the total_tiles x sk_ktn k-steps; partial tiles meet through sk_slots / sk_flags
@@ -149,6 +162,9 @@ struct GemmParams {
   // columns, row stride ldc; peers' buffers reached over NVLink with plain stores), L = 1
   int n_out;
   unsigned long long outs[8];
+  // dense: 1 = C is stored with TMA (tensor map tm_c; N % 8 == 0, C 16-byte aligned, one
+  // output buffer); grouped: decided per group from its n and C address
+  int c_tma;
   // fused epilogue (dense): out = act(acc + bias[n]) stored as fp16 or bf16
   const float* bias;            // per output column n, or null
   int act;                      // 0 none, 1 relu, 2 gelu (erf form)
@@ -167,6 +183,8 @@ struct TileInfo {
   int p_rows, q_rows, K;
   const void* map_p;
   const void* map_q;
+  const void* map_c;     // C store map (TMA epilogue)
+  bool c_tma;
   const uint8_t* sf_p;   // batch-adjusted base
   const uint8_t* sf_q;
   __half* C;             // batch-adjusted base
@@ -218,7 +236,8 @@ __device__ __forceinline__ bool seg_next(const GemmParams& prm, int total, int w
 
 template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false>
 __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtensorMap* tm_p,
-                                            const CUtensorMap* tm_q, int t, TileInfo& ti) {
+                                            const CUtensorMap* tm_q, const CUtensorMap* tm_c, int t,
+                                            TileInfo& ti) {
   if constexpr (!GROUPED) {
     const int per_batch = prm.tiles_p * prm.tiles_q;
     const int l = t / per_batch;
@@ -235,6 +254,8 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtenso
     ti.K = prm.K;
     ti.map_p = tm_p;
     ti.map_q = tm_q;
+    ti.map_c = tm_c;
+    ti.c_tma = prm.c_tma != 0;
     ti.sf_p = prm.sf_p + (long long)l * prm.sf_p_batch;
     ti.sf_q = prm.sf_q + (long long)l * prm.sf_q_batch;
     ti.C = prm.C + (long long)l * prm.c_batch;
@@ -258,17 +279,20 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtenso
     const int tq = (m + BN - 1) / BN;
     const int qb = r % tq;
     const int pb = r / tq;
-    ti.p0 = pb * kBM;
+    // a CTA pair covers 256 rows of B_g; this CTA owns rows [p0, p0 + 128)
+    ti.p0 = CTA2 ? pb * 2 * kBM + (int)cluster_ctarank() * kBM : pb * kBM;
     ti.q0 = qb * BN;
     ti.l = 0;
     ti.p_rows = n;
     ti.q_rows = m;
     ti.K = k;
-    ti.map_p = prm.maps + 2 * g;
-    ti.map_q = prm.maps + 2 * g + 1;
+    ti.map_p = prm.maps + 3 * g;
+    ti.map_q = prm.maps + 3 * g + 1;
+    ti.map_c = prm.maps + 3 * g + 2;
     ti.sf_p = reinterpret_cast<const uint8_t*>(__ldg(prm.sfs + 2 * g + 1));
     ti.sf_q = reinterpret_cast<const uint8_t*>(__ldg(prm.sfs + 2 * g + 0));
     ti.C = reinterpret_cast<__half*>(__ldg(prm.abc + 3 * g + 2));
+    ti.c_tma = (n & 7) == 0 && (reinterpret_cast<uintptr_t>(ti.C) & 15) == 0;
     ti.ldc = n;
     ti.rk = (k + 63) / 64;
     ti.num_kt = (k + KB * 64 - 1) / (KB * 64);
@@ -302,8 +326,7 @@ template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false, bool SK = 
 __global__ void __launch_bounds__(kNumThreads, 1)
 nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constant__ CUtensorMap tm_q,
                   const __grid_constant__ CUtensorMap tm_sfp, const __grid_constant__ CUtensorMap tm_sfq,
-                  const GemmParams prm) {
-  static_assert(!(CTA2 && GROUPED), "CTA pairs are used for the dense GEMM only");
+                  const __grid_constant__ CUtensorMap tm_c, const GemmParams prm) {
   static_assert(!SK || (!GROUPED && !CTA2 && BN <= 128), "stream-K: dense, 1-CTA, BN <= 128");
   using C_ = Cfg<BN, KB, CTA2>;
   constexpr int S = C_::kStages;
@@ -314,22 +337,26 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_addr);
 
-  // [stage 0 .. S-1: P | Q] [scale slot 0 .. NS-1: SFP atoms | SFQ atoms] [barriers]
+  // [stage 0 .. S-1: P | Q] [epilogue staging] [scale slot 0 .. NS-1: SFP | SFQ atoms]
+  // [barriers]
   constexpr int NS = C_::kSfSlots;
-  constexpr int LEAD = C_::kSfLead;
+  constexpr int T = C_::kSfBufs;
   auto stage_off = [&](int s) { return (uint32_t)(s * C_::kStageBytes); };
   constexpr uint32_t kOffQ = C_::kPBytes;
-  constexpr uint32_t kSlot0 = S * C_::kStageBytes;
+  constexpr uint32_t kEpi0 = S * C_::kStageBytes;
+  constexpr uint32_t kSlot0 = kEpi0 + C_::kEpiBytes;
   auto slot_off = [&](int j) { return kSlot0 + (uint32_t)(j * C_::kSfSlotBytes); };
   constexpr uint32_t kOffSfq = C_::kSfpBytes;  // within a slot
   const uint32_t bar_base = base + kSlot0 + NS * C_::kSfSlotBytes;
   auto full_bar = [&](int s) { return bar_base + 8 * s; };
-  auto sff_bar = [&](int s) { return bar_base + 8 * (S + s); };  // scales of stage s in TMEM
-  auto empty_bar = [&](int s) { return bar_base + 8 * (2 * S + s); };
-  auto accf_bar = [&](int a) { return bar_base + 8 * (3 * S + a); };
-  auto acce_bar = [&](int a) { return bar_base + 8 * (3 * S + A + a); };
-  const uint32_t drain_bar = bar_base + 8 * (3 * S + 2 * A);
-  auto sfd_bar = [&](int j) { return bar_base + 8 * (3 * S + 2 * A + 1 + j); };
+  auto empty_bar = [&](int s) { return bar_base + 8 * (S + s); };
+  auto sff_bar = [&](int t) { return bar_base + 8 * (2 * S + t); };      // scales in TMEM buffer t
+  auto sfe_bar = [&](int t) { return bar_base + 8 * (2 * S + T + t); };  // TMEM buffer t free
+  auto accf_bar = [&](int a) { return bar_base + 8 * (2 * S + 2 * T + a); };
+  auto acce_bar = [&](int a) { return bar_base + 8 * (2 * S + 2 * T + A + a); };
+  const uint32_t drain_bar = bar_base + 8 * (2 * S + 2 * T + 2 * A);
+  auto sfd_bar = [&](int j) { return bar_base + 8 * (2 * S + 2 * T + 2 * A + 1 + j); };       // slot landed
+  auto sfs_bar = [&](int j) { return bar_base + 8 * (2 * S + 2 * T + 2 * A + 1 + NS + j); };  // slot free
   uint8_t* bar_ptr = smem + kSlot0 + NS * C_::kSfSlotBytes;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bar_ptr + 8 * C_::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + 8 * C_::kNumBars + 4);
@@ -353,15 +380,21 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     // one per epilogue warp
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
-      mbar_init(sff_bar(s), CTA2 ? 8 : 4);
       mbar_init(empty_bar(s), 1);
+    }
+    for (int t = 0; t < T; ++t) {
+      mbar_init(sff_bar(t), CTA2 ? 8 : 4);
+      mbar_init(sfe_bar(t), 1);
     }
     for (int a = 0; a < A; ++a) {
       mbar_init(accf_bar(a), 1);
       mbar_init(acce_bar(a), kEpiWarps * (CTA2 ? 2 : 1));
     }
     mbar_init(drain_bar, 1);
-    for (int j = 0; j < NS; ++j) mbar_init(sfd_bar(j), 1);
+    for (int j = 0; j < NS; ++j) {
+      mbar_init(sfd_bar(j), 1);
+      mbar_init(sfs_bar(j), 4);  // the 4 scale warps (of this CTA) that moved the slot's atoms
+    }
     *abort_flag = 0;
     fence_mbar_init();
     fence_async_shared();
@@ -371,6 +404,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_sfp);
     prefetch_tmap(&tm_sfq);
+    prefetch_tmap(&tm_c);
     // Pull this CTA's first k-stages into L2 while the previous kernel finishes: an L2
     // prefetch is safe before the wait on that kernel even if it writes these inputs
     // (L2 is the point of coherence, nothing lands in this SM).  Dense only: the grouped
@@ -378,7 +412,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     Seg sg0;
     if (seg_first<SK>(prm, prm.total_tiles, work0, work_step, sg0)) {
       TileInfo ti;
-      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg0.t, ti);
+      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, sg0.t, ti);
       const int kte = min(sg0.kt1, ti.num_kt);
       for (int kt = sg0.kt0 + (warp - kProducerWarp); kt < sg0.kt0 + S && kt < kte; kt += kNumProducers) {
         tma_prefetch_l2_3d(&tm_p, kt * C_::kBKBytes, ti.p0, ti.l);
@@ -423,11 +457,31 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     return kbv > KB ? KB : kbv;
   };
 
+  // Cursor over this CTA's k-steps (tile, k-stage), for the scale loads issued ahead.
+  struct Cursor {
+    Seg sg;
+    int kt, kte;
+    bool valid;
+    TileInfo ti;
+  };
+  auto cur_load = [&](Cursor& c) {
+    if (!c.valid) return;
+    decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, c.sg.t, c.ti);
+    c.kt = c.sg.kt0;
+    c.kte = min(c.sg.kt1, c.ti.num_kt);
+  };
+  auto cur_next = [&](Cursor& c) {
+    if (++c.kt == c.kte) {
+      c.valid = seg_next<SK>(prm, total, work0, work_step, c.sg);
+      cur_load(c);
+    }
+  };
+
   if (warp >= kProducerWarp && warp < kProducerWarp + kNumProducers) {
     if (lane == 0 && !(prm.debug & 1)) {
       // ------------------------------------------------------------ producers
-      // Producer j issues the loads of k-steps j, j + 2, ...: one thread issuing TMA and
-      // bulk copies tops out at about one 28 KB stage per ~250 ns, two double that.
+      // Producer p issues the operand loads of k-steps p, p + 3, ...: one thread issuing TMA
+      // copies tops out at about one stage per ~250 ns.
       const uint32_t pid = warp - kProducerWarp;
       uint32_t gstep = 0;
       const uint64_t pol_keep = policy_evict_last();
@@ -436,71 +490,11 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       const void* last_map = nullptr;
       bool ok = true;
       uint32_t issued_mask = 0, issued_par = 0;
-      // Cursor over this CTA's k-steps (tile, k-stage) LEAD steps ahead of the operand
-      // loads: the scale atoms of that step go into its slot of the scale ring.
-      struct Cursor {
-        Seg sg;
-        int kt, kte;
-        bool valid;
-        TileInfo ti;
-      };
-      auto cur_load = [&](Cursor& c) {
-        if (!c.valid) return;
-        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, c.sg.t, c.ti);
-        c.kt = c.sg.kt0;
-        c.kte = min(c.sg.kt1, c.ti.num_kt);
-      };
-      auto cur_next = [&](Cursor& c) {
-        if (++c.kt == c.kte) {
-          c.valid = seg_next<SK>(prm, total, work0, work_step, c.sg);
-          cur_load(c);
-        }
-      };
-      Cursor sfc;
-      sfc.valid = seg_first<SK>(prm, total, work0, work_step, sfc.sg);
-      cur_load(sfc);
-      int sl = 0;
-      uint32_t slph = 0;
-      uint32_t sf_issued = 0, sf_par = 0;
-      auto issue_sf = [&](const Cursor& c) {
-        const uint32_t bar = sfd_bar(sl);
-        const uint32_t dst = base + slot_off(sl);
-        if constexpr (!GROUPED) {
-          // two tensor loads (one per operand's scale blocks; out-of-range atoms read as
-          // zero and are ignored): a tensor load costs the issuing thread ~50 cycles, a
-          // plain bulk copy ~115
-          mbar_arrive_expect_tx(bar, C_::kSfSlotBytes);
-          tma_load_3d(dst, &tm_sfp, bar, c.kt * KB * 64, c.ti.p0 >> 7, c.ti.l, pol_keep);
-          tma_load_3d(dst + kOffSfq, &tm_sfq, bar, c.kt * KB * 64, c.ti.q0 >> 7, c.ti.l, pol_keep);
-          sf_issued |= 1u << sl;
-          sf_par = (sf_par & ~(1u << sl)) | (slph << sl);
-          return;
-        }
-        const uint32_t sf_bytes = k_blocks(c.ti, c.kt) * kAtomBytes;
-        const int nq = q_atoms(c.ti);
-        mbar_arrive_expect_tx(bar, sf_bytes * (1 + nq));
-        bulk_load(dst, c.ti.sf_p + ((long long)(c.ti.p0 >> 7) * c.ti.rk + c.kt * KB) * kAtomBytes,
-                  sf_bytes, bar, pol_keep);
-        for (int a = 0; a < nq; ++a)
-          bulk_load(dst + kOffSfq + a * KB * kAtomBytes,
-                    c.ti.sf_q + ((long long)((c.ti.q0 >> 7) + a) * c.ti.rk + c.kt * KB) * kAtomBytes,
-                    sf_bytes, bar, pol_keep);
-        sf_issued |= 1u << sl;
-        sf_par = (sf_par & ~(1u << sl)) | (slph << sl);
-      };
-      auto sf_step = [&](bool mine) {  // the cursor's step: issue if it is ours, then advance
-        if (!sfc.valid) return;
-        if (mine) issue_sf(sfc);
-        if (++sl == NS) { sl = 0; slph ^= 1; }
-        cur_next(sfc);
-      };
-      // scale atoms of steps 0 .. LEAD-1 go out first (their slots are fresh)
-      for (int j = 0; j < LEAD; ++j) sf_step(j % kNumProducers == (int)pid);
       Seg sg;
       for (bool more = seg_first<SK>(prm, total, work0, work_step, sg); more && ok;
            more = seg_next<SK>(prm, total, work0, work_step, sg)) {
         TileInfo ti;
-        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg.t, ti);
+        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, sg.t, ti);
         if (GROUPED && ti.map_p != last_map) {
           tmap_fence_acquire(ti.map_p);
           tmap_fence_acquire(ti.map_q);
@@ -508,34 +502,29 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         }
         const int kte = min(sg.kt1, ti.num_kt);
         for (int kt = sg.kt0; kt < kte; ++kt, ++gstep) {
-          const bool mine = gstep % kNumProducers == pid;
-          if (mine) {
-            // stage s free: the MMAs of step gstep - S are done (and with them every read
-            // of the scale slot step gstep + LEAD reuses)
+          if (gstep % kNumProducers == pid) {
+            // stage s free: the MMAs of step gstep - S are done
             if (!mbar_wait_bounded(empty_bar(s), ph ^ 1, abort_flag, prm.status,
                                    kStatusTimeoutProducer, tmo)) { ok = false; break; }
-            {
-              const uint32_t st = base + stage_off(s);
-              if constexpr (CTA2) {
-                // both CTAs' tiles count on the leader's full barrier, which the MMA waits on
-                if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * (C_::kPBytes + C_::kQBytes));
-                const uint32_t fb = mapa_shared(full_bar(s), 0);
-                tma_load_3d_pair(st, ti.map_p, fb, kt * C_::kBKBytes, ti.p0, ti.l, pol_keep);
-                tma_load_3d_pair(st + kOffQ, ti.map_q, fb, kt * C_::kBKBytes,
-                                 ti.q0 + (int)crank * C_::kQRows, ti.l, pol_keep);
-              } else {
-                mbar_arrive_expect_tx(full_bar(s), C_::kPBytes + C_::kQBytes);
-                tma_load_3d(st, ti.map_p, full_bar(s), kt * C_::kBKBytes, ti.p0, ti.l, pol_keep);
-                tma_load_3d(st + kOffQ, ti.map_q, full_bar(s), kt * C_::kBKBytes,
-                            ti.q0 + (int)crank * C_::kQRows, ti.l, pol_keep);
-              }
-              if (!CTA2 || leader) {  // (a peer cannot wait on the leader's barrier)
-                issued_mask |= 1u << s;
-                issued_par = (issued_par & ~(1u << s)) | (ph << s);
-              }
+            const uint32_t st = base + stage_off(s);
+            if constexpr (CTA2) {
+              // both CTAs' tiles count on the leader's full barrier, which the MMA waits on
+              if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * (C_::kPBytes + C_::kQBytes));
+              const uint32_t fb = mapa_shared(full_bar(s), 0);
+              tma_load_3d_pair(st, ti.map_p, fb, kt * C_::kBKBytes, ti.p0, ti.l, pol_keep);
+              tma_load_3d_pair(st + kOffQ, ti.map_q, fb, kt * C_::kBKBytes,
+                               ti.q0 + (int)crank * C_::kQRows, ti.l, pol_keep);
+            } else {
+              mbar_arrive_expect_tx(full_bar(s), C_::kPBytes + C_::kQBytes);
+              tma_load_3d(st, ti.map_p, full_bar(s), kt * C_::kBKBytes, ti.p0, ti.l, pol_keep);
+              tma_load_3d(st + kOffQ, ti.map_q, full_bar(s), kt * C_::kBKBytes,
+                          ti.q0 + (int)crank * C_::kQRows, ti.l, pol_keep);
+            }
+            if (!CTA2 || leader) {  // (a peer cannot wait on the leader's barrier)
+              issued_mask |= 1u << s;
+              issued_par = (issued_par & ~(1u << s)) | (ph << s);
             }
           }
-          sf_step(mine);
           if (++s == S) { s = 0; ph ^= 1; }
         }
       }
@@ -544,9 +533,6 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         for (int i = 0; i < S; ++i)
           if (issued_mask & (1u << i))
             mbar_wait_plain(full_bar(i), (issued_par >> i) & 1u, 100000000ull);
-        for (int i = 0; i < NS; ++i)
-          if (sf_issued & (1u << i))
-            mbar_wait_plain(sfd_bar(i), (sf_par >> i) & 1u, 100000000ull);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -557,12 +543,13 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       uint32_t aph = 0;
       int s = 0;
       uint32_t ph = 0;
-      uint32_t step = 0;
+      int t = 0;  // TMEM scale buffer
+      uint32_t tph = 0;
       Seg sg;
       for (bool more = seg_first<SK>(prm, total, work0, work_step, sg); more && ok;
            more = seg_next<SK>(prm, total, work0, work_step, sg)) {
         TileInfo ti;
-        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg.t, ti);
+        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, sg.t, ti);
         const int kte = min(sg.kt1, ti.num_kt);
         // A pair splits the instruction's N in halves between the two CTAs' shared memory,
         // so it always issues N = BN (each CTA staged BN/2 rows; rows past the edge are zero).
@@ -578,16 +565,16 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         if (!mbar_wait_bounded(acce_bar(acc), aph ^ 1, abort_flag, prm.status, kStatusTimeoutMma,
                                tmo)) { ok = false; break; }
         tc_fence_after();
-        for (int kt = sg.kt0; kt < kte; ++kt, ++step) {
+        for (int kt = sg.kt0; kt < kte; ++kt) {
           // the operand tiles landed (a pair's full barrier counts both CTAs' bytes) and
-          // the stage's scales are in TMEM
+          // the step's scales are in TMEM buffer t
           if (!mbar_wait_bounded(full_bar(s), ph, abort_flag, prm.status, kStatusTimeoutMma, tmo) ||
-              !mbar_wait_bounded(sff_bar(s), ph, abort_flag, prm.status, kStatusTimeoutMma, tmo)) {
+              !mbar_wait_bounded(sff_bar(t), tph, abort_flag, prm.status, kStatusTimeoutMma, tmo)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sfp_col = tmem_base + C_::kSfCol0 + s * C_::kSfCols;
+          const uint32_t sfp_col = tmem_base + C_::kSfCol0 + t * C_::kSfCols;
           const uint32_t sfq_col = sfp_col + C_::kSfpCols + sfq_shift;
           const uint64_t pdesc = make_smem_desc(base + stage_off(s), 0, C_::kSbo, C_::kSwizzle);
           const uint64_t qdesc = make_smem_desc(base + stage_off(s) + kOffQ, 0, C_::kSbo, C_::kSwizzle);
@@ -613,9 +600,16 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
                                 sfq_col + kb * C_::kSfqColsPerKb, kb > 0 ? 1u : acc0);
             }
           }
-          // release the stage (and its scale buffer) once these MMAs have read it
-          if (CTA2) tc_commit_2cta(empty_bar(s)); else tc_commit(empty_bar(s));
+          // release the stage and the TMEM scale buffer once these MMAs have read them
+          if (CTA2) {
+            tc_commit_2cta(empty_bar(s));
+            tc_commit_2cta(sfe_bar(t));
+          } else {
+            tc_commit(empty_bar(s));
+            tc_commit(sfe_bar(t));
+          }
           if (++s == S) { s = 0; ph ^= 1; }
+          if (++t == T) { t = 0; tph ^= 1; }
         }
         if (!ok) break;
         if (CTA2) tc_commit_2cta(accf_bar(acc)); else tc_commit(accf_bar(acc));
@@ -666,29 +660,69 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       tmem_st_32x32b(col, r.p);
       tmem_st_32x32b(col + C_::kSfpCols, r.q);
     };
-    // Group g serves the k-steps j with j % 2 == g.  Per step: wait until the step's TMEM
-    // scale buffer is free (the MMAs of step j - S are done) and its scale atoms landed in
-    // their slot, write them, and arrive on the stage's sf_full (the leader's, for a pair).
+    // Group g serves the k-steps j with j % 2 == g.  Per step: wait until TMEM scale buffer
+    // j % T is free (the MMAs of step j - T are done) and the step's scale atoms landed in
+    // slot j % NS, write them, then free the slot and arrive on the buffer's sf_full (the
+    // leader's, for a pair).
+    // The scale atoms are loaded by the group itself: lane 0 of its first warp issues the
+    // loads of the group's own steps into the group's own slots (NS is even, so slot j % NS
+    // always belongs to the group of step j), NS steps ahead, and refills a slot as soon as
+    // the group's four warps have read it (sf_free).  No other thread waits on these slots,
+    // and no operand producer ever waits for a scale copy.
+    const bool issuer = (warp & 3) == 0 && lane == 0 && !(prm.debug & 1);
+    const uint64_t pol_keep = policy_evict_last();
+    uint32_t sf_issued = 0, sf_par = 0;  // slots with a load issued, and that load's phase
+    Cursor ic;                            // issue cursor (issuer only): global step istep
+    int istep = 0;
+    auto issue_sf = [&](const Cursor& c, int slot, uint32_t par) {
+      const uint32_t bar = sfd_bar(slot);
+      const uint32_t dst = base + slot_off(slot);
+      if constexpr (!GROUPED) {
+        // two tensor loads (one per operand's scale blocks; out-of-range atoms read as zero
+        // and are ignored)
+        mbar_arrive_expect_tx(bar, C_::kSfSlotBytes);
+        tma_load_3d(dst, &tm_sfp, bar, c.kt * KB * 64, c.ti.p0 >> 7, c.ti.l, pol_keep);
+        tma_load_3d(dst + kOffSfq, &tm_sfq, bar, c.kt * KB * 64, c.ti.q0 >> 7, c.ti.l, pol_keep);
+      } else {
+        const uint32_t sf_bytes = k_blocks(c.ti, c.kt) * kAtomBytes;
+        const int nq = q_atoms(c.ti);
+        mbar_arrive_expect_tx(bar, sf_bytes * (1 + nq));
+        bulk_load(dst, c.ti.sf_p + ((long long)(c.ti.p0 >> 7) * c.ti.rk + c.kt * KB) * kAtomBytes,
+                  sf_bytes, bar, pol_keep);
+        for (int a = 0; a < nq; ++a)
+          bulk_load(dst + kOffSfq + a * KB * kAtomBytes,
+                    c.ti.sf_q + ((long long)((c.ti.q0 >> 7) + a) * c.ti.rk + c.kt * KB) * kAtomBytes,
+                    sf_bytes, bar, pol_keep);
+      }
+      sf_issued |= 1u << slot;
+      sf_par = (sf_par & ~(1u << slot)) | (par << slot);
+    };
+    if (issuer) {  // the group's first NS / 2 steps (steps 0 .. NS-1 of its parity)
+      ic.valid = seg_first<SK>(prm, total, work0, work_step, ic.sg);
+      cur_load(ic);
+      for (; istep < NS && ic.valid; ++istep, cur_next(ic))
+        if ((istep & 1) == grp) issue_sf(ic, istep, 0u);
+    }
     int sl = 0;
     uint32_t slph = 0;
     Seg sg;
     for (bool more = seg_first<SK>(prm, total, work0, work_step, sg); more && ok;
          more = seg_next<SK>(prm, total, work0, work_step, sg)) {
       TileInfo ti;
-      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg.t, ti);
+      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, sg.t, ti);
       const int nq_atoms = q_atoms(ti);
       const int kte = min(sg.kt1, ti.num_kt);
       for (int kt = sg.kt0; kt < kte && ok; ++kt, ++tstep) {
         const int cs = s;
         const uint32_t cph = ph;
-        if (++s == S) { s = 0; ph ^= 1; }
+        if (++s == T) { s = 0; ph ^= 1; }
         const int cslot = sl;
         const uint32_t cslph = slph;
         if (++sl == NS) { sl = 0; slph ^= 1; }
         if ((int)(tstep & 1) != grp) continue;
         int w_ok = 1;
         if (lane == 0)
-          w_ok = mbar_wait_bounded(empty_bar(cs), cph ^ 1, abort_flag, prm.status,
+          w_ok = mbar_wait_bounded(sfe_bar(cs), cph ^ 1, abort_flag, prm.status,
                                    kStatusTimeoutMma, tmo) &&
                  mbar_wait_bounded(sfd_bar(cslot), cslph, abort_flag, prm.status,
                                    kStatusTimeoutMma, tmo);
@@ -703,16 +737,43 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) arrive_leader(sff_bar(cs));
+        if (lane == 0) {
+          mbar_arrive(sfs_bar(cslot));
+          arrive_leader(sff_bar(cs));
+        }
+        int i_ok = 1;
+        if (issuer) {
+          // refill the slot with step tstep + NS once the group's four warps have read it
+          while (ic.valid && istep < (int)tstep + NS) {
+            cur_next(ic);
+            ++istep;
+          }
+          if (ic.valid) {
+            if (mbar_wait_bounded(sfs_bar(cslot), cslph, abort_flag, prm.status,
+                                  kStatusTimeoutMma, tmo))
+              issue_sf(ic, cslot, cslph ^ 1u);
+            else
+              i_ok = 0;
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, i_ok, 0)) { ok = false; break; }
       }
+    }
+    if (issuer && *abort_flag) {
+      // let the scale loads already issued land before the CTA exits (bounded)
+      for (int i = 0; i < NS; ++i)
+        if (sf_issued & (1u << i))
+          mbar_wait_plain(sfd_bar(i), (sf_par >> i) & 1u, 100000000ull);
     }
     }
   } else {
     {
     // -------------------------------------------------------------- epilogue
     // Warp w owns accumulator rows 32*(w%4).. and columns [h*BN/2, (h+1)*BN/2), h = w/4.
-    // It pulls its whole slice out of TMEM as packed fp16 first, releases the
-    // accumulator, and only then writes global memory.
+    // It pulls its slice out of TMEM as packed fp16 (two 32-column chunks at a time),
+    // releases the accumulator after the last load, and writes C with TMA stores: each
+    // 16-column piece goes through one of the warp's 1 KB staging buffers in shared memory
+    // (double-buffered where they fit) and leaves with one bulk tensor store.
     constexpr int kHalf = BN / 2;
     constexpr int kChunks = kHalf / 32;
     constexpr int kPhase = kChunks > 2 ? 2 : kChunks;  // chunks drained per store phase
@@ -721,11 +782,13 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     const int quad = warp & 3;
     const int half = warp >> 2;
     const int row = quad * 32 + lane;  // TMEM lane == accumulator row
+    const uint32_t epi_buf0 = base + kEpi0 + (uint32_t)(warp * C_::kEpiBufs) * 1024u;
+    uint32_t epi_n = 0;  // staging buffers used so far (rotation)
     Seg sg;
     for (bool more = seg_first<SK>(prm, total, work0, work_step, sg); more;
          more = seg_next<SK>(prm, total, work0, work_step, sg)) {
       TileInfo ti;
-      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, sg.t, ti);
+      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, sg.t, ti);
       if (!mbar_wait_bounded(accf_bar(acc), aph, abort_flag, prm.status, kStatusTimeoutEpilogue,
                              tmo)) break;
       tc_fence_after();
@@ -768,9 +831,55 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
           }
         }
       };
+      // TMA store of chunks c0 .. c0 + kPhase - 1 in 16-column pieces.  Non-swapped: the
+      // piece is 32 rows (lanes) x 16 columns, 32-byte rows, 32-byte swizzle.  Swapped
+      // (C = D^T): 16 rows of C (the piece's q) x 32 columns (lanes), 64-byte rows, 64-byte
+      // swizzle.  Rows and columns past C's edges are clipped by the TMA unit.
+      const int row0 = ti.p0 + quad * 32;
+      auto store_tma = [&](const uint32_t (&pk)[kPhase][16], int c0) {
+#pragma unroll
+        for (int c = 0; c < kPhase; ++c) {
+          const int qc = q_lo + (c0 + c) * 32;
+          if (c0 + c >= kChunks || qc >= ti.q_rows) break;  // warp-uniform
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            if (qc + hh * 16 >= ti.q_rows) break;
+            const uint32_t buf = epi_buf0 + (C_::kEpiBufs == 2 ? (epi_n & 1u) * 1024u : 0u);
+            ++epi_n;
+            // the buffer's previous store has finished reading it
+            if (lane == 0) bulk_wait_group_read<C_::kEpiBufs - 1>();
+            __syncwarp();
+            if constexpr (!SWAP) {
+              const uint32_t rb = buf + (uint32_t)lane * 32u;
+              const uint32_t sw = ((uint32_t)lane >> 2) & 1u;
+              st_shared_v4(rb + (sw << 4), pk[c][hh * 8 + 0], pk[c][hh * 8 + 1], pk[c][hh * 8 + 2],
+                           pk[c][hh * 8 + 3]);
+              st_shared_v4(rb + ((sw ^ 1u) << 4), pk[c][hh * 8 + 4], pk[c][hh * 8 + 5],
+                           pk[c][hh * 8 + 6], pk[c][hh * 8 + 7]);
+            } else {
+              const uint32_t col = (((uint32_t)lane & 7u) << 1);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const uint32_t v = pk[c][hh * 8 + (j >> 1)];
+                const uint32_t chunk = (((uint32_t)lane >> 3) ^ (((uint32_t)j >> 1) & 3u)) << 4;
+                st_shared_u16(buf + (uint32_t)j * 64u + chunk + col,
+                              (uint16_t)((j & 1) ? (v >> 16) : (v & 0xffffu)));
+              }
+            }
+            fence_async_shared();  // make the generic-proxy writes visible to the TMA unit
+            __syncwarp();
+            if (lane == 0) {
+              if constexpr (!SWAP) tma_store_3d(ti.map_c, buf, qc + hh * 16, row0, ti.l);
+              else tma_store_3d(ti.map_c, buf, row0, qc + hh * 16, ti.l);
+              bulk_commit_group();
+            }
+          }
+        }
+      };
       auto store_all = [&](const uint32_t (&pk)[kPhase][16], int c0) {
         if (prm.n_out == 0) {
-          store_c(ti.C, pk, c0);
+          if (ti.c_tma) store_tma(pk, c0);
+          else store_c(ti.C, pk, c0);
         } else {
 #pragma unroll
           for (int d = 0; d < 8; ++d)
@@ -947,6 +1056,8 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         store_all(pk, c0);
       }
     }
+    // the CTA's shared memory must outlive the TMA stores that read it
+    if (lane == 0) bulk_wait_group_all();
     }
   }
 

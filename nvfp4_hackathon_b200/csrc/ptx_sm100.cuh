@@ -403,7 +403,34 @@ __device__ __forceinline__ void tc_commit_2cta(uint32_t bar) {
       "h"(mask)
       : "memory");
 }
-// try_wait that acquires at cluster scope (for phases completed by the peer CTA).
+// ---------------------------------------------------------------- TMA stores
+// 3-D tiled store shared -> global (x = innermost element index, y = row, z = batch), in a
+// bulk-async group; elements outside the tensor's extents are not written.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until at most N committed bulk groups of this thread are still reading shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until every committed bulk group of this thread has completed (writes performed).
+__device__ __forceinline__ void bulk_wait_group_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
 
 // Named barrier among a subset of warps (id 1..15).
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {

@@ -2,10 +2,12 @@
 
 ``quantize(x)`` turns real-valued activations or weights into exactly the tensors the
 GEMM entry points take: packed e2m1 codes, plain e4m3 block scales and the same scales
-in the permuted layout.  It is the reference's input generation
-(kernels/gemm/reference.py:86-150 -- per-16-element amax / 6 -> e4m3 scale, nearest e2m1,
-``to_blocked``) done by one HBM-bound kernel instead of a chain of torch ops; the
-rounding rules are those of ``inputs.quantize_nvfp4``, bit for bit.
+in the permuted layout.  The quantisation rule is the one the benchmark configurations
+specify for their inputs (fp32 values -> per-16-element amax / 6 -> e4m3 scale -> nearest
+e2m1 code, ties to even; restated on the host by ``inputs.quantize_nvfp4``, which this
+kernel matches bit for bit).  The reference itself draws random codes and small integer
+scales instead of quantising values; from it comes only the permuted scale layout
+(``to_blocked``, kernels/gemm/reference.py:13-24 and :113-150).
 """
 from __future__ import annotations
 

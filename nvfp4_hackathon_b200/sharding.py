@@ -157,6 +157,9 @@ def gemm_allgather(data, peers: PeerBuffers, col_lo: int, n_full: int, stream=No
     ``data`` is this rank's 7-tuple (L = 1; B holds the rank's n columns); its c is unused.
     The peers may read their buffers only after every rank's kernel: follow with a
     stream-ordered collective (``dist.all_reduce`` of a 1-element tensor) or a barrier.
+    The kernel also writes into every peer's buffer, so when peers read their C between
+    two calls, order each call after those reads as well (the same collective or barrier
+    before the call): otherwise the next call's stores race with a peer still reading.
     """
     import torch
     from . import _native

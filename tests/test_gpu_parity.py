@@ -179,20 +179,22 @@ REF_GROUP_CASES = [
 ]
 
 
-@pytest.mark.parametrize("bn,stage_k", [(64, 0), (128, 0), (192, 0), (256, 0), (128, 128)])
+@pytest.mark.parametrize("bn,stage_k,pair", [(64, 0, 0), (128, 0, 0), (192, 0, 0), (256, 0, 0),
+                                             (128, 128, 0), (128, 0, 2), (256, 0, 2)])
 @pytest.mark.parametrize("case", range(len(REF_GROUP_CASES)))
-def test_reference_group_cases(cuda, case, bn, stage_k):
+def test_reference_group_cases(cuda, case, bn, stage_k, pair):
     m, n, k = REF_GROUP_CASES[case]
     gdata = inputs.generate_group_input(m, n, k, len(m), seed=1111)
-    got = _run_grouped(gdata, opt=_native.options(tile_n=bn, stage_k=stage_k))
+    got = _run_grouped(gdata, opt=_native.options(tile_n=bn, stage_k=stage_k, cta_pair=pair))
     for g, (x, e) in enumerate(zip(got, _grouped_expected(gdata))):
         assert_close(x, e, f"case {case} group {g}")
 
 
-def test_grouped_config3(cuda):
+@pytest.mark.parametrize("pair", [0, 2])
+def test_grouped_config3(cuda, pair):
     ms = inputs.uniform_group_sizes(8, seed=1111)
     gdata = inputs.generate_quantized_group_input(ms, 4096, 7168, seed=1111)
-    got = _run_grouped(gdata)
+    got = _run_grouped(gdata, opt=_native.options(cta_pair=pair, tile_n=256 if pair else 0))
     for g, (x, e) in enumerate(zip(got, _grouped_expected(gdata))):
         assert_close(x, e, f"c3 group {g}")
 

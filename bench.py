@@ -257,7 +257,7 @@ class Workload:
         else:
             n, k = w["n"], w["k"]
             if self.kind == "grouped":
-                ms = inputs.uniform_group_sizes(w["g"], seed=seed)
+                ms = inputs.uniform_group_sizes(w["g"], seed=1111)  # same sizes in every input copy
                 self.scaling = "weak"
                 self.global_flops = grouped_flops(ms, n, k) * world
                 local = ms

@@ -145,7 +145,9 @@ struct GemmParams {
   long long ldc;                // elements between rows of C
   long long c_batch;            // elements between batches of C
   int tiles_p, tiles_q, total_tiles;
-  int q_fastest;                // raster order: 1 = walk Q tiles first
+  // raster: bands of band_p P tiles; within a band the P tiles vary fastest, then the Q
+  // tiles, so the concurrent tiles share one band of P rows (kept in L2) while Q streams
+  int band_p;
   // grouped problem
   int G;
   const int* sizes;             // G x 4: m, n, k, l
@@ -243,8 +245,13 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtenso
     const int l = t / per_batch;
     const int r = t - l * per_batch;
     int pb, qb;
-    if (prm.q_fastest) { qb = r % prm.tiles_q; pb = r / prm.tiles_q; }
-    else               { pb = r % prm.tiles_p; qb = r / prm.tiles_p; }
+    const int per_band = prm.band_p * prm.tiles_q;
+    const int band = r / per_band;
+    const int rb = r - band * per_band;
+    const int p_first = band * prm.band_p;
+    const int gb = min(prm.band_p, prm.tiles_p - p_first);
+    pb = p_first + rb % gb;
+    qb = rb / gb;
     // a CTA pair covers 256 P rows; this CTA owns rows [p0, p0 + 128)
     ti.p0 = CTA2 ? pb * 2 * kBM + (int)cluster_ctarank() * kBM : pb * kBM;
     ti.q0 = qb * BN;

@@ -500,7 +500,7 @@ __global__ void __launch_bounds__(kMaxGroups)
 nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_constant__ CUtensorMap tmpl_q,
                    const __grid_constant__ CUtensorMap tmpl_c, const int* __restrict__ sizes, const unsigned long long* __restrict__ abc,
                    const unsigned long long* __restrict__ sfs, int G, CUtensorMap* maps,
-                   int* prefix, int pm, int bn, int* status) {
+                   int* prefix, int pm, int bn, int swap, int* status) {
   __shared__ int warp_sums[kMaxGroups / 32];
   pdl_launch_dependents();
   // the workspace may still be read by the previous call's GEMM on this stream
@@ -518,22 +518,25 @@ nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_cons
     if (!valid) {
       atomicCAS(status, 0, 5 /* NVFP4_STATUS_BAD_GROUP */);
     } else if (!empty) {
-      tiles = ((n + pm - 1) / pm) * ((m + bn - 1) / bn);  // (pm = 256 for CTA pairs)
+      // (pm = 256 for CTA pairs; swapped: B_g rows on the pm side, tokens on the bn side)
+      tiles = swap ? ((n + pm - 1) / pm) * ((m + bn - 1) / bn) : ((m + pm - 1) / pm) * ((n + bn - 1) / bn);
       CUtensorMap* mp = maps + 3 * g;
       CUtensorMap* mq = maps + 3 * g + 1;
       *mp = tmpl_p;
       *mq = tmpl_q;
       const uint64_t kbytes = (uint64_t)k / 2;
-      tmap_replace_addr(mp, reinterpret_cast<const void*>(pb));
+      const unsigned long long p_ptr = swap ? pb : pa, q_ptr = swap ? pa : pb;
+      const uint32_t p_rows = (uint32_t)(swap ? n : m), q_rows = (uint32_t)(swap ? m : n);
+      tmap_replace_addr(mp, reinterpret_cast<const void*>(p_ptr));
       tmap_replace_dim<0>(mp, (uint32_t)kbytes);
-      tmap_replace_dim<1>(mp, (uint32_t)n);
+      tmap_replace_dim<1>(mp, p_rows);
       tmap_replace_stride<0>(mp, kbytes);
-      tmap_replace_stride<1>(mp, kbytes * (uint64_t)n);
-      tmap_replace_addr(mq, reinterpret_cast<const void*>(pa));
+      tmap_replace_stride<1>(mp, kbytes * (uint64_t)p_rows);
+      tmap_replace_addr(mq, reinterpret_cast<const void*>(q_ptr));
       tmap_replace_dim<0>(mq, (uint32_t)kbytes);
-      tmap_replace_dim<1>(mq, (uint32_t)m);
+      tmap_replace_dim<1>(mq, q_rows);
       tmap_replace_stride<0>(mq, kbytes);
-      tmap_replace_stride<1>(mq, kbytes * (uint64_t)m);
+      tmap_replace_stride<1>(mq, kbytes * (uint64_t)q_rows);
       if ((n & 7) == 0 && (pc & 15ull) == 0) {
         CUtensorMap* mc = maps + 3 * g + 2;
         *mc = tmpl_c;
@@ -572,7 +575,7 @@ nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_cons
   if (g == 0) prefix[0] = 0;
 }
 
-template <int BN, int KB = 4, bool CTA2 = false>
+template <int BN, int KB = 4, bool CTA2 = false, bool SWAP = true>
 int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sfs, int G, void* ws,
                    cudaStream_t stream, DeviceState* st, const nvfp4_options* opt) {
   // Templates: any valid 16-byte-aligned address and sizes; the prep kernel
@@ -583,7 +586,7 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   rc = encode_operand_map(&tq, ws, 128, 128, 1, CTA2 ? BN / 2 : BN, KB * 32);
   if (rc) return rc;
   CUtensorMap tc;
-  rc = encode_c_map(&tc, ws, 64, 64, 1, /*swap=*/true);
+  rc = encode_c_map(&tc, ws, 64, 64, 1, SWAP);
   if (rc) return rc;
   CUtensorMap* maps = static_cast<CUtensorMap*>(ws);
   int* prefix = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) +
@@ -592,7 +595,7 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   cudaError_t e = launch_pdl(nvfp4_grouped_prep, dim3(1), dim3(threads), 0, stream, 1, false, tp, tq, tc, sizes,
                              reinterpret_cast<const unsigned long long*>(abc),
                              reinterpret_cast<const unsigned long long*>(sfs), G, maps, prefix,
-                             CTA2 ? 2 * kBM : kBM, BN,
+                             CTA2 ? 2 * kBM : kBM, BN, SWAP ? 1 : 0,
                              (opt && opt->dev_status) ? opt->dev_status : st->status);
   if (e != cudaSuccess) return cuda_fail(e, "nvfp4_grouped_prep launch");
   GemmParams prm;
@@ -611,7 +614,7 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   if (CTA2) grid = grid / 2 < 1 ? 2 : grid / 2 * 2;  // whole pairs
   // (the grouped kernel copies scales with plain bulk copies: the scale maps are unused, and
   // its operand and C maps are the per-group ones in the workspace)
-  return launch<true, true, BN, KB, CTA2>(tp, tq, tp, tq, tc, prm, grid, stream);
+  return launch<true, SWAP, BN, KB, CTA2>(tp, tq, tp, tq, tc, prm, grid, stream);
 }
 
 }  // namespace
@@ -793,6 +796,18 @@ int nvfp4_grouped_gemm_ex(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int bn = (opt && opt->tile_n > 0) ? opt->tile_n : kGroupedBN;
+  if (opt && opt->operand_order == 1) {
+    // A_g (tokens) on the 128-row MMA side, B_g rows on the N side: tiles of 128 tokens x bn
+    // rows of B_g (or 256 tokens on a CTA pair); fewer MMA instructions than the swapped
+    // order when groups hold many tokens, since only the last 128-token tile is padded
+    if (opt->cta_pair == 2 && bn == 256)
+      return run_grouped_bn<256, 4, true, false>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
+    if (opt->cta_pair != 2 && bn == 256)
+      return run_grouped_bn<256, 4, false, false>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
+    if (opt->cta_pair != 2 && bn == 128)
+      return run_grouped_bn<128, 4, false, false>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
+    return fail(NVFP4_ERR_UNSUPPORTED, "grouped operand_order 1 is built for tile_n 128, 256 (pair: 256)");
+  }
   if (opt && opt->cta_pair == 2) {  // 256 rows of B_g per tile on a CTA pair
     if (bn == 128) return run_grouped_bn<128, 4, true>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
     if (bn == 256) return run_grouped_bn<256, 4, true>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);

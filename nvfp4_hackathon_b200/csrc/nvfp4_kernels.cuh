@@ -282,22 +282,25 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtenso
     const int n = __ldg(prm.sizes + 4 * g + 1);
     const int k = __ldg(prm.sizes + 4 * g + 2);
     const int r = t - __ldg(prm.tile_prefix + g);
-    // swap layout: P = B_g (n rows), Q = A_g (m rows); walk Q (token) tiles first
-    const int tq = (m + BN - 1) / BN;
+    // swapped: P = B_g (n rows), Q = A_g (m token rows); otherwise P = A_g, Q = B_g.  The
+    // tiles of a group are walked Q first (the concurrent tiles share P rows).
+    const int prow = SWAP ? n : m;
+    const int qrow = SWAP ? m : n;
+    const int tq = (qrow + BN - 1) / BN;
     const int qb = r % tq;
     const int pb = r / tq;
-    // a CTA pair covers 256 rows of B_g; this CTA owns rows [p0, p0 + 128)
+    // a CTA pair covers 256 P rows; this CTA owns rows [p0, p0 + 128)
     ti.p0 = CTA2 ? pb * 2 * kBM + (int)cluster_ctarank() * kBM : pb * kBM;
     ti.q0 = qb * BN;
     ti.l = 0;
-    ti.p_rows = n;
-    ti.q_rows = m;
+    ti.p_rows = prow;
+    ti.q_rows = qrow;
     ti.K = k;
     ti.map_p = prm.maps + 3 * g;
     ti.map_q = prm.maps + 3 * g + 1;
     ti.map_c = prm.maps + 3 * g + 2;
-    ti.sf_p = reinterpret_cast<const uint8_t*>(__ldg(prm.sfs + 2 * g + 1));
-    ti.sf_q = reinterpret_cast<const uint8_t*>(__ldg(prm.sfs + 2 * g + 0));
+    ti.sf_p = reinterpret_cast<const uint8_t*>(__ldg(prm.sfs + 2 * g + (SWAP ? 1 : 0)));
+    ti.sf_q = reinterpret_cast<const uint8_t*>(__ldg(prm.sfs + 2 * g + (SWAP ? 0 : 1)));
     ti.C = reinterpret_cast<__half*>(__ldg(prm.abc + 3 * g + 2));
     ti.c_tma = (n & 7) == 0 && (reinterpret_cast<uintptr_t>(ti.C) & 15) == 0;
     ti.ldc = n;
@@ -693,9 +696,13 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       } else {
         const uint32_t sf_bytes = k_blocks(c.ti, c.kt) * kAtomBytes;
         const int nq = q_atoms(c.ti);
-        mbar_arrive_expect_tx(bar, sf_bytes * (1 + nq));
-        bulk_load(dst, c.ti.sf_p + ((long long)(c.ti.p0 >> 7) * c.ti.rk + c.kt * KB) * kAtomBytes,
-                  sf_bytes, bar, pol_keep);
+        // (the second CTA of a pair can lie wholly past the P rows, e.g. a group of fewer than
+        // 129 tokens: its scale block does not exist and its rows are never stored)
+        const int np = c.ti.p0 < c.ti.p_rows ? 1 : 0;
+        mbar_arrive_expect_tx(bar, sf_bytes * (np + nq));
+        if (np)
+          bulk_load(dst, c.ti.sf_p + ((long long)(c.ti.p0 >> 7) * c.ti.rk + c.kt * KB) * kAtomBytes,
+                    sf_bytes, bar, pol_keep);
         for (int a = 0; a < nq; ++a)
           bulk_load(dst + kOffSfq + a * KB * kAtomBytes,
                     c.ti.sf_q + ((long long)((c.ti.q0 >> 7) + a) * c.ti.rk + c.kt * KB) * kAtomBytes,

@@ -103,6 +103,32 @@ def choose_tile_n(sizes, num_sms: int) -> int:
     return best
 
 
+def _mma_waves(sizes, num_sms: int, tokens_on_m: bool, bn: int) -> int:
+    """(waves of tiles over the SMs) x (k-stages per tile): the MMA instructions of a tile run
+    one after another at a fixed cost each (the same for every N up to 256), so this counts
+    the tensor-pipe time of the call."""
+    tiles, kt = 0, 0
+    for m, n, k, _ in sizes:
+        if m <= 0 or n <= 0:
+            continue
+        tiles += (-(-m // 128) * -(-n // bn)) if tokens_on_m else (-(-n // 128) * -(-m // bn))
+        kt = max(kt, -(-k // 256))
+    return (-(-tiles // num_sms)) * kt if tiles else 0
+
+
+def choose_order(sizes, num_sms: int) -> tuple[int, int]:
+    """(operand_order, tile_n) for a call without options: tokens on the 128-row MMA side with
+    256 rows of B_g per tile (order 1) when that needs fewer MMA waves than the swapped order
+    (B_g on the 128-row side) at its best token width; otherwise the swapped order.  Measured
+    on B200: configs[3] 79.8 vs 92.8 us, configs[4a] 319.6 vs 335 us, the reference's case 1
+    (N=7168, K=2048) 30.9 vs 36.9 us with order 1; its cases 0, 2, 3 (ties in this count)
+    41.8 / 15.5 / 11.0 us swapped against 45.9 / 17.8 / 12.4."""
+    bn = choose_tile_n(sizes, num_sms)
+    if _mma_waves(sizes, num_sms, True, 256) < _mma_waves(sizes, num_sms, False, bn):
+        return 1, 256
+    return 0, bn
+
+
 def custom_kernel(data: group_input_t, opt=None) -> group_output_t:
     abc, _, sfp, sizes = data
     if len(abc) == 0:
@@ -127,6 +153,11 @@ def custom_kernel(data: group_input_t, opt=None) -> group_output_t:
             sms = _SM_COUNT[device.index] = torch.cuda.get_device_properties(device).multi_processor_count
         if opt is None:
             opt = _native.options()
-        opt.tile_n = choose_tile_n(sizes, sms)
+        if opt.operand_order == 0 and opt.cta_pair == 0:
+            opt.operand_order, opt.tile_n = choose_order(sizes, sms)
+        elif opt.operand_order == 1 or opt.cta_pair == 2:
+            opt.tile_n = 256
+        else:
+            opt.tile_n = choose_tile_n(sizes, sms)
     launch_tables(table, len(sizes), opt=opt)
     return [c for _, _, c in abc]

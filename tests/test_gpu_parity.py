@@ -181,20 +181,25 @@ REF_GROUP_CASES = [
 
 @pytest.mark.parametrize("bn,stage_k,pair", [(64, 0, 0), (128, 0, 0), (192, 0, 0), (256, 0, 0),
                                              (128, 128, 0), (128, 0, 2), (256, 0, 2)])
+@pytest.mark.parametrize("order", [0, 1])
 @pytest.mark.parametrize("case", range(len(REF_GROUP_CASES)))
-def test_reference_group_cases(cuda, case, bn, stage_k, pair):
+def test_reference_group_cases(cuda, case, order, bn, stage_k, pair):
+    if order == 1 and not ((bn == 256 and stage_k == 0) or (bn == 128 and stage_k == 0 and pair == 0)):
+        pytest.skip("tokens-on-M grouped kernel is built for tile_n 128 and 256 (pair: 256)")
     m, n, k = REF_GROUP_CASES[case]
     gdata = inputs.generate_group_input(m, n, k, len(m), seed=1111)
-    got = _run_grouped(gdata, opt=_native.options(tile_n=bn, stage_k=stage_k, cta_pair=pair))
+    got = _run_grouped(gdata, opt=_native.options(tile_n=bn, stage_k=stage_k, cta_pair=pair,
+                                                  operand_order=order))
     for g, (x, e) in enumerate(zip(got, _grouped_expected(gdata))):
         assert_close(x, e, f"case {case} group {g}")
 
 
-@pytest.mark.parametrize("pair", [0, 2])
-def test_grouped_config3(cuda, pair):
+@pytest.mark.parametrize("pair,order", [(0, 0), (2, 0), (0, 1), (2, 1)])
+def test_grouped_config3(cuda, pair, order):
     ms = inputs.uniform_group_sizes(8, seed=1111)
     gdata = inputs.generate_quantized_group_input(ms, 4096, 7168, seed=1111)
-    got = _run_grouped(gdata, opt=_native.options(cta_pair=pair, tile_n=256 if pair else 0))
+    got = _run_grouped(gdata, opt=_native.options(cta_pair=pair, tile_n=256 if (pair or order) else 0,
+                                                  operand_order=order))
     for g, (x, e) in enumerate(zip(got, _grouped_expected(gdata))):
         assert_close(x, e, f"c3 group {g}")
 
@@ -211,6 +216,17 @@ def test_grouped_config4a_sampled(cuda):
                                    u8(sa[:, :, 0].contiguous())[rows],
                                    u8(sb[:, :, 0].contiguous()))], dtype=np.float32)[0]
         assert_close(got[g][rows], e, f"c4a group {g}")
+
+
+@pytest.mark.parametrize("order", [0, 1])
+def test_grouped_pairs_past_the_edge(cuda, order):
+    """CTA pairs whose second CTA lies wholly past the 128-row side: groups of 16..128 tokens
+    (tokens on that side) and B_g of 384 rows (B_g on that side)."""
+    ms = [16, 48, 128, 130, 0, 272]
+    gdata = inputs.generate_group_input(ms, [384] * 6, [512] * 6, 6, seed=21)
+    got = _run_grouped(gdata, opt=_native.options(tile_n=256, cta_pair=2, operand_order=order))
+    for g, (x, e) in enumerate(zip(got, _grouped_expected(gdata))):
+        assert_close(x, e, f"order {order} group {g}")
 
 
 def test_grouped_empty_groups_and_reuse(cuda):

@@ -173,7 +173,7 @@ int nvfp4_quantize(const void* x, int dtype, int rows, int k, int l, void* codes
  * nvfp4_grouped_gemm wants.  Same tables, same results as nvfp4_grouped_gemm
  * with default options.
  * Limit: 1 <= G <= 256 (larger G is rejected with NVFP4_ERR_UNSUPPORTED).
- * The scratch (about 97 KiB for the per-group tensor maps and tile schedule) is
+ * The scratch (about 161 KiB for the per-group tensor maps and tile schedule) is
  * a fixed device array inside the library; each GPU that loads the library
  * holds it until the process exits.  The first call on a device looks up that
  * array's address (with that device current); make that first call before any

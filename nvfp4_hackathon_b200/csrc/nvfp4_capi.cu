@@ -371,11 +371,6 @@ int run_dense_bn(const void* a, const void* b, const void* sfa, const void* sfb,
   prm.q_rows = q_rows;
   prm.K = k;
   prm.L = l;
-  const long long rk = (k + 63) / 64;
-  prm.sf_p = static_cast<const uint8_t*>(sfP);
-  prm.sf_q = static_cast<const uint8_t*>(sfQ);
-  prm.sf_p_batch = (long long)((p_rows + 127) / 128) * rk * kAtomBytes;
-  prm.sf_q_batch = (long long)((q_rows + 127) / 128) * rk * kAtomBytes;
   prm.C = static_cast<__half*>(c);
   prm.ldc = n;
   if (g_multi_out) {
@@ -468,7 +463,7 @@ constexpr int kGroupedBN = 256;
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 size_t grouped_ws_bytes(int G) {
-  return align_up((size_t)G * 3 * sizeof(CUtensorMap), 256) + align_up((size_t)(G + 1) * 4, 256);
+  return align_up((size_t)G * 5 * sizeof(CUtensorMap), 256) + align_up((size_t)(G + 1) * 4, 256);
 }
 
 __device__ __forceinline__ void tmap_replace_addr(void* m, const void* p) {
@@ -498,7 +493,9 @@ __device__ __forceinline__ void tmap_replace_stride(void* m, uint64_t v) {
 // per-group tile counts into the schedule prefix.
 __global__ void __launch_bounds__(kMaxGroups)
 nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_constant__ CUtensorMap tmpl_q,
-                   const __grid_constant__ CUtensorMap tmpl_c, const int* __restrict__ sizes, const unsigned long long* __restrict__ abc,
+                   const __grid_constant__ CUtensorMap tmpl_c, const __grid_constant__ CUtensorMap tmpl_sfp,
+                   const __grid_constant__ CUtensorMap tmpl_sfq, const int* __restrict__ sizes,
+                   const unsigned long long* __restrict__ abc,
                    const unsigned long long* __restrict__ sfs, int G, CUtensorMap* maps,
                    int* prefix, int pm, int bn, int swap, int* status) {
   __shared__ int warp_sums[kMaxGroups / 32];
@@ -520,8 +517,8 @@ nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_cons
     } else if (!empty) {
       // (pm = 256 for CTA pairs; swapped: B_g rows on the pm side, tokens on the bn side)
       tiles = swap ? ((n + pm - 1) / pm) * ((m + bn - 1) / bn) : ((m + pm - 1) / pm) * ((n + bn - 1) / bn);
-      CUtensorMap* mp = maps + 3 * g;
-      CUtensorMap* mq = maps + 3 * g + 1;
+      CUtensorMap* mp = maps + 5 * g;
+      CUtensorMap* mq = maps + 5 * g + 1;
       *mp = tmpl_p;
       *mq = tmpl_q;
       const uint64_t kbytes = (uint64_t)k / 2;
@@ -537,8 +534,28 @@ nvfp4_grouped_prep(const __grid_constant__ CUtensorMap tmpl_p, const __grid_cons
       tmap_replace_dim<1>(mq, q_rows);
       tmap_replace_stride<0>(mq, kbytes);
       tmap_replace_stride<1>(mq, kbytes * (uint64_t)q_rows);
+      // scale maps: permuted scales as 8-byte elements, row = one 128-row block
+      {
+        const uint64_t rk = (uint64_t)k / 64;
+        const unsigned long long sp = swap ? sb : sa, sq = swap ? sa : sb;
+        const uint32_t bp = (p_rows + 127) / 128, bq = (q_rows + 127) / 128;
+        CUtensorMap* ms = maps + 5 * g + 3;
+        CUtensorMap* mt = maps + 5 * g + 4;
+        *ms = tmpl_sfp;
+        *mt = tmpl_sfq;
+        tmap_replace_addr(ms, reinterpret_cast<const void*>(sp));
+        tmap_replace_dim<0>(ms, (uint32_t)(rk * 64));
+        tmap_replace_dim<1>(ms, bp);
+        tmap_replace_stride<0>(ms, rk * kAtomBytes);
+        tmap_replace_stride<1>(ms, rk * kAtomBytes * bp);
+        tmap_replace_addr(mt, reinterpret_cast<const void*>(sq));
+        tmap_replace_dim<0>(mt, (uint32_t)(rk * 64));
+        tmap_replace_dim<1>(mt, bq);
+        tmap_replace_stride<0>(mt, rk * kAtomBytes);
+        tmap_replace_stride<1>(mt, rk * kAtomBytes * bq);
+      }
       if ((n & 7) == 0 && (pc & 15ull) == 0) {
-        CUtensorMap* mc = maps + 3 * g + 2;
+        CUtensorMap* mc = maps + 5 * g + 2;
         *mc = tmpl_c;
         tmap_replace_addr(mc, reinterpret_cast<const void*>(pc));
         tmap_replace_dim<0>(mc, (uint32_t)n);
@@ -588,11 +605,16 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   CUtensorMap tc;
   rc = encode_c_map(&tc, ws, 64, 64, 1, SWAP);
   if (rc) return rc;
+  CUtensorMap tsp, tsq;  // scale-map templates: the box (one k-stage of 1 or 2 blocks) is kept
+  rc = encode_sf_map(&tsp, ws, 128, 256, 1, KB, 1);
+  if (rc) return rc;
+  rc = encode_sf_map(&tsq, ws, 256, 256, 1, KB, Cfg<BN, KB, CTA2>::kSfqAtoms);
+  if (rc) return rc;
   CUtensorMap* maps = static_cast<CUtensorMap*>(ws);
   int* prefix = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) +
-                                       align_up((size_t)G * 3 * sizeof(CUtensorMap), 256));
+                                       align_up((size_t)G * 5 * sizeof(CUtensorMap), 256));
   const int threads = ((G + 31) / 32) * 32;
-  cudaError_t e = launch_pdl(nvfp4_grouped_prep, dim3(1), dim3(threads), 0, stream, 1, false, tp, tq, tc, sizes,
+  cudaError_t e = launch_pdl(nvfp4_grouped_prep, dim3(1), dim3(threads), 0, stream, 1, false, tp, tq, tc, tsp, tsq, sizes,
                              reinterpret_cast<const unsigned long long*>(abc),
                              reinterpret_cast<const unsigned long long*>(sfs), G, maps, prefix,
                              CTA2 ? 2 * kBM : kBM, BN, SWAP ? 1 : 0,
@@ -612,9 +634,8 @@ int run_grouped_bn(const int32_t* sizes, const uint64_t* abc, const uint64_t* sf
   int grid = st->num_sms;
   if (opt && opt->max_ctas > 0 && opt->max_ctas < grid) grid = opt->max_ctas;
   if (CTA2) grid = grid / 2 < 1 ? 2 : grid / 2 * 2;  // whole pairs
-  // (the grouped kernel copies scales with plain bulk copies: the scale maps are unused, and
-  // its operand and C maps are the per-group ones in the workspace)
-  return launch<true, SWAP, BN, KB, CTA2>(tp, tq, tp, tq, tc, prm, grid, stream);
+  // (the grouped kernel's operand, scale and C maps are the per-group ones in the workspace)
+  return launch<true, SWAP, BN, KB, CTA2>(tp, tq, tsp, tsq, tc, prm, grid, stream);
 }
 
 }  // namespace
@@ -802,6 +823,8 @@ int nvfp4_grouped_gemm_ex(const int32_t* sizes_dev, const uint64_t* abc_ptrs_dev
     // order when groups hold many tokens, since only the last 128-token tile is padded
     if (opt->cta_pair == 2 && bn == 256)
       return run_grouped_bn<256, 4, true, false>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
+    if (opt->cta_pair != 2 && bn == 256 && opt->stage_k == 128)
+      return run_grouped_bn<256, 2, false, false>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
     if (opt->cta_pair != 2 && bn == 256)
       return run_grouped_bn<256, 4, false, false>(sizes_dev, abc_ptrs_dev, sf_ptrs_dev, G, workspace, s, st, opt);
     if (opt->cta_pair != 2 && bn == 128)
@@ -863,13 +886,13 @@ int nvfp4_quantize(const void* x, int dtype, int rows, int k, int l, void* codes
 
 // ------------------------------------------------------------------ grouped GEMM without allocation
 // Scratch for nvfp4_grouped_gemm_noalloc: room for the per-group tensor maps and
-// the tile prefix of up to kNoAllocMaxGroups groups (about 97 KiB).  Every GPU
+// the tile prefix of up to kNoAllocMaxGroups groups (about 161 KiB).  Every GPU
 // that loads the library holds one copy until the process exits.  In host code
 // the name below is only a host-side stand-in; the device address comes from
 // cudaGetSymbolAddress, once per device.
 constexpr int kNoAllocMaxGroups = 256;
 constexpr size_t kNoAllocScratchBytes =
-    ((size_t)kNoAllocMaxGroups * 3 * sizeof(CUtensorMap) + 255) / 256 * 256 +
+    ((size_t)kNoAllocMaxGroups * 5 * sizeof(CUtensorMap) + 255) / 256 * 256 +
     ((size_t)(kNoAllocMaxGroups + 1) * 4 + 255) / 256 * 256;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

@@ -137,10 +137,6 @@ struct Cfg {
 struct GemmParams {
   // dense problem (ignored when grouped)
   int p_rows, q_rows, K, L;
-  const uint8_t* sf_p;          // permuted scale factors of P
-  const uint8_t* sf_q;          // permuted scale factors of Q
-  long long sf_p_batch;         // bytes between batches
-  long long sf_q_batch;
   __half* C;
   long long ldc;                // elements between rows of C
   long long c_batch;            // elements between batches of C
@@ -153,7 +149,7 @@ struct GemmParams {
   const int* sizes;             // G x 4: m, n, k, l
   const unsigned long long* abc;  // G x 3: a, b, c
   const unsigned long long* sfs;  // G x 2: sfa (permuted), sfb (permuted)
-  const CUtensorMap* maps;      // G x 3: [P map = B_g, Q map = A_g, C_g store map]
+  const CUtensorMap* maps;      // G x 5: [P operand, Q operand, C_g store, P scales, Q scales]
   const int* tile_prefix;       // G + 1 running tile counts
   // stream-K (dense only): when sk_ktn > 0 every CTA takes an equal contiguous range of
   // the total_tiles x sk_ktn k-steps; partial tiles meet through sk_slots / sk_flags
@@ -186,9 +182,9 @@ struct TileInfo {
   const void* map_p;
   const void* map_q;
   const void* map_c;     // C store map (TMA epilogue)
+  const void* map_sfp;   // scale maps of P and Q (8-byte elements: row = 128-row block)
+  const void* map_sfq;
   bool c_tma;
-  const uint8_t* sf_p;   // batch-adjusted base
-  const uint8_t* sf_q;
   __half* C;             // batch-adjusted base
   long long ldc;
   int rk;                // 64-wide K blocks (atoms per 128-row block)
@@ -238,7 +234,8 @@ __device__ __forceinline__ bool seg_next(const GemmParams& prm, int total, int w
 
 template <bool GROUPED, bool SWAP, int BN, int KB, bool CTA2 = false>
 __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtensorMap* tm_p,
-                                            const CUtensorMap* tm_q, const CUtensorMap* tm_c, int t,
+                                            const CUtensorMap* tm_q, const CUtensorMap* tm_c,
+                                            const CUtensorMap* tm_sfp, const CUtensorMap* tm_sfq, int t,
                                             TileInfo& ti) {
   if constexpr (!GROUPED) {
     const int per_batch = prm.tiles_p * prm.tiles_q;
@@ -262,9 +259,9 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtenso
     ti.map_p = tm_p;
     ti.map_q = tm_q;
     ti.map_c = tm_c;
+    ti.map_sfp = tm_sfp;
+    ti.map_sfq = tm_sfq;
     ti.c_tma = prm.c_tma != 0;
-    ti.sf_p = prm.sf_p + (long long)l * prm.sf_p_batch;
-    ti.sf_q = prm.sf_q + (long long)l * prm.sf_q_batch;
     ti.C = prm.C + (long long)l * prm.c_batch;
     ti.ldc = prm.ldc;
     ti.rk = (prm.K + 63) / 64;
@@ -296,11 +293,11 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& prm, const CUtenso
     ti.p_rows = prow;
     ti.q_rows = qrow;
     ti.K = k;
-    ti.map_p = prm.maps + 3 * g;
-    ti.map_q = prm.maps + 3 * g + 1;
-    ti.map_c = prm.maps + 3 * g + 2;
-    ti.sf_p = reinterpret_cast<const uint8_t*>(__ldg(prm.sfs + 2 * g + (SWAP ? 1 : 0)));
-    ti.sf_q = reinterpret_cast<const uint8_t*>(__ldg(prm.sfs + 2 * g + (SWAP ? 0 : 1)));
+    ti.map_p = prm.maps + 5 * g;
+    ti.map_q = prm.maps + 5 * g + 1;
+    ti.map_c = prm.maps + 5 * g + 2;
+    ti.map_sfp = prm.maps + 5 * g + 3;
+    ti.map_sfq = prm.maps + 5 * g + 4;
     ti.C = reinterpret_cast<__half*>(__ldg(prm.abc + 3 * g + 2));
     ti.c_tma = (n & 7) == 0 && (reinterpret_cast<uintptr_t>(ti.C) & 15) == 0;
     ti.ldc = n;
@@ -422,7 +419,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     Seg sg0;
     if (seg_first<SK>(prm, prm.total_tiles, work0, work_step, sg0)) {
       TileInfo ti;
-      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, sg0.t, ti);
+      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, &tm_sfp, &tm_sfq, sg0.t, ti);
       const int kte = min(sg0.kt1, ti.num_kt);
       for (int kt = sg0.kt0 + (warp - kProducerWarp); kt < sg0.kt0 + S && kt < kte; kt += kNumProducers) {
         tma_prefetch_l2_3d(&tm_p, kt * C_::kBKBytes, ti.p0, ti.l);
@@ -476,7 +473,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
   };
   auto cur_load = [&](Cursor& c) {
     if (!c.valid) return;
-    decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, c.sg.t, c.ti);
+    decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, &tm_sfp, &tm_sfq, c.sg.t, c.ti);
     c.kt = c.sg.kt0;
     c.kte = min(c.sg.kt1, c.ti.num_kt);
   };
@@ -504,7 +501,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       for (bool more = seg_first<SK>(prm, total, work0, work_step, sg); more && ok;
            more = seg_next<SK>(prm, total, work0, work_step, sg)) {
         TileInfo ti;
-        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, sg.t, ti);
+        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, &tm_sfp, &tm_sfq, sg.t, ti);
         if (GROUPED && ti.map_p != last_map) {
           tmap_fence_acquire(ti.map_p);
           tmap_fence_acquire(ti.map_q);
@@ -559,7 +556,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       for (bool more = seg_first<SK>(prm, total, work0, work_step, sg); more && ok;
            more = seg_next<SK>(prm, total, work0, work_step, sg)) {
         TileInfo ti;
-        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, sg.t, ti);
+        decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, &tm_sfp, &tm_sfq, sg.t, ti);
         const int kte = min(sg.kt1, ti.num_kt);
         // A pair splits the instruction's N in halves between the two CTAs' shared memory,
         // so it always issues N = BN (each CTA staged BN/2 rows; rows past the edge are zero).
@@ -683,31 +680,21 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     const uint64_t pol_keep = policy_evict_last();
     uint32_t sf_issued = 0, sf_par = 0;  // slots with a load issued, and that load's phase
     Cursor ic;                            // issue cursor (issuer only): global step istep
+    const void* last_sf_map = nullptr;
     int istep = 0;
     auto issue_sf = [&](const Cursor& c, int slot, uint32_t par) {
       const uint32_t bar = sfd_bar(slot);
       const uint32_t dst = base + slot_off(slot);
-      if constexpr (!GROUPED) {
-        // two tensor loads (one per operand's scale blocks; out-of-range atoms read as zero
-        // and are ignored)
-        mbar_arrive_expect_tx(bar, C_::kSfSlotBytes);
-        tma_load_3d(dst, &tm_sfp, bar, c.kt * KB * 64, c.ti.p0 >> 7, c.ti.l, pol_keep);
-        tma_load_3d(dst + kOffSfq, &tm_sfq, bar, c.kt * KB * 64, c.ti.q0 >> 7, c.ti.l, pol_keep);
-      } else {
-        const uint32_t sf_bytes = k_blocks(c.ti, c.kt) * kAtomBytes;
-        const int nq = q_atoms(c.ti);
-        // (the second CTA of a pair can lie wholly past the P rows, e.g. a group of fewer than
-        // 129 tokens: its scale block does not exist and its rows are never stored)
-        const int np = c.ti.p0 < c.ti.p_rows ? 1 : 0;
-        mbar_arrive_expect_tx(bar, sf_bytes * (np + nq));
-        if (np)
-          bulk_load(dst, c.ti.sf_p + ((long long)(c.ti.p0 >> 7) * c.ti.rk + c.kt * KB) * kAtomBytes,
-                    sf_bytes, bar, pol_keep);
-        for (int a = 0; a < nq; ++a)
-          bulk_load(dst + kOffSfq + a * KB * kAtomBytes,
-                    c.ti.sf_q + ((long long)((c.ti.q0 >> 7) + a) * c.ti.rk + c.kt * KB) * kAtomBytes,
-                    sf_bytes, bar, pol_keep);
+      // two tensor loads (one per operand's scale blocks; out-of-range atoms read as zero
+      // and are ignored); the grouped GEMM's per-group scale maps come from the prep kernel
+      if (GROUPED && c.ti.map_sfp != last_sf_map) {
+        tmap_fence_acquire(c.ti.map_sfp);
+        tmap_fence_acquire(c.ti.map_sfq);
+        last_sf_map = c.ti.map_sfp;
       }
+      mbar_arrive_expect_tx(bar, C_::kSfSlotBytes);
+      tma_load_3d(dst, c.ti.map_sfp, bar, c.kt * KB * 64, c.ti.p0 >> 7, c.ti.l, pol_keep);
+      tma_load_3d(dst + kOffSfq, c.ti.map_sfq, bar, c.kt * KB * 64, c.ti.q0 >> 7, c.ti.l, pol_keep);
       sf_issued |= 1u << slot;
       sf_par = (sf_par & ~(1u << slot)) | (par << slot);
     };
@@ -723,7 +710,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     for (bool more = seg_first<SK>(prm, total, work0, work_step, sg); more && ok;
          more = seg_next<SK>(prm, total, work0, work_step, sg)) {
       TileInfo ti;
-      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, sg.t, ti);
+      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, &tm_sfp, &tm_sfq, sg.t, ti);
       const int nq_atoms = q_atoms(ti);
       const int kte = min(sg.kt1, ti.num_kt);
       for (int kt = sg.kt0; kt < kte && ok; ++kt, ++tstep) {
@@ -798,11 +785,12 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     const int row = quad * 32 + lane;  // TMEM lane == accumulator row
     const uint32_t epi_buf0 = base + kEpi0 + (uint32_t)(warp * C_::kEpiBufs) * 1024u;
     uint32_t epi_n = 0;  // staging buffers used so far (rotation)
+    const void* last_c_map = nullptr;
     Seg sg;
     for (bool more = seg_first<SK>(prm, total, work0, work_step, sg); more;
          more = seg_next<SK>(prm, total, work0, work_step, sg)) {
       TileInfo ti;
-      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, sg.t, ti);
+      decode_tile<GROUPED, SWAP, BN, KB, CTA2>(prm, &tm_p, &tm_q, &tm_c, &tm_sfp, &tm_sfq, sg.t, ti);
       if (!mbar_wait_bounded(accf_bar(acc), aph, abort_flag, prm.status, kStatusTimeoutEpilogue,
                              tmo)) break;
       tc_fence_after();
@@ -850,6 +838,10 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
       // (C = D^T): 16 rows of C (the piece's q) x 32 columns (lanes), 64-byte rows, 64-byte
       // swizzle.  Rows and columns past C's edges are clipped by the TMA unit.
       const int row0 = ti.p0 + quad * 32;
+      if (GROUPED && ti.c_tma && lane == 0 && ti.map_c != last_c_map) {
+        tmap_fence_acquire(ti.map_c);  // written by the prep kernel through the generic proxy
+        last_c_map = ti.map_c;
+      }
       auto store_tma = [&](const uint32_t (&pk)[kPhase][16], int c0) {
 #pragma unroll
         for (int c = 0; c < kPhase; ++c) {

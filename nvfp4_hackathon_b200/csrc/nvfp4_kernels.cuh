@@ -777,7 +777,10 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
     // (double-buffered where they fit) and leaves with one bulk tensor store.
     constexpr int kHalf = BN / 2;
     constexpr int kChunks = kHalf / 32;
-    constexpr int kPhase = kChunks > 2 ? 2 : kChunks;  // chunks drained per store phase
+    // chunks drained per store phase: the whole slice in the non-swapped order (the
+    // accumulator is free before the first store), two chunks (32 registers) in the swapped
+    // order, whose per-lane store addressing needs more registers (it spilled with four)
+    constexpr int kPhase = (!SWAP || kChunks <= 2) ? kChunks : 2;
     int acc = 0;
     uint32_t aph = 0;
     const int quad = warp & 3;
@@ -1020,7 +1023,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_p, const __grid_constan
         }
       }
       // Drain kPhase chunks of 32 columns into registers as packed fp16/bf16, store them,
-      // then the next kPhase: at most 2 chunks (32 registers) are live.  The accumulator is
+      // then the next kPhase.  The accumulator is
       // released right after its last TMEM load; the MMAs of the next tile wait at most
       // for the issue of the earlier phases' stores (fire-and-forget).
 #pragma unroll

@@ -51,8 +51,11 @@ extern "C" {
 /* Tuning / test knobs; zero-initialise and set what you need. */
 typedef struct nvfp4_options {
   int operand_order;              /* 0 = auto; 1 = A feeds the 128-row MMA side;
-                                     2 = B feeds it ("swap", for skinny M) */
-  int tile_n;                     /* 0 = auto; else 64, 128 or 256 */
+                                     2 = B feeds it ("swap", for skinny M).  Grouped GEMM:
+                                     0 / 2 = B_g on the 128-row side, tokens on the N side;
+                                     1 = tokens (A_g) on the 128-row side, tile_n 128 or 256
+                                     rows of B_g on the N side (256 with cta_pair = 2) */
+  int tile_n;                     /* 0 = library default; else 64, 128 or 256 (grouped: also 192) */
   int max_ctas;                   /* 0 = one CTA per SM */
   unsigned long long timeout_ns;  /* 0 = library default (2 s per pipeline wait) */
   int debug;                      /* test bit, 0 in normal use: 1 = issue no loads, so every
@@ -62,7 +65,9 @@ typedef struct nvfp4_options {
                                      that this call's kernels record their first error into
                                      (atomicCAS from 0: the caller clears it before the call) */
   int stage_k;                    /* 0 = auto; 128 or 256 K elements per pipeline stage */
-  int cta_pair;                   /* 0 = auto, 1 = off, 2 = M=256 tiles on a CTA pair (cta_group::2) */
+  int cta_pair;                   /* 0 = auto (dense: pairs for M >= 256 with N >= 2048), 1 = off,
+                                     2 = 256-row tiles on a CTA pair (cta_group::2; grouped:
+                                     tile_n 128 or 256) */
   int stream_k;                   /* dense: 0 / 1 = off, 2 = on (k-steps split evenly over all SMs).  Stream-K
                                      keeps a per-stream workspace (flags + fp32 partials, ~16 MiB),
                                      allocated by the first stream-K call on that stream (outside

@@ -3,7 +3,7 @@
 Same tuple layouts as the reference's task contracts:
 kernels/gemm/task.py:4-5 (7-tuple) and kernels/group_gemm/task.py:4-5 (4-tuple of lists).
 """
-from typing import TypedDict, TypeVar
+from typing import TypeVar
 
 import torch
 
@@ -23,15 +23,3 @@ group_input_t = TypeVar(
                 list[tuple[int, int, int, int]]])
 group_output_t = TypeVar("group_output_t", bound=list[torch.Tensor])
 
-
-class GemmSpec(TypedDict):
-    m: int
-    n: int
-    k: int
-    l: int
-    seed: int
-
-
-class GroupSpec(TypedDict):
-    problem_sizes: list[tuple[int, int, int, int]]
-    seed: int

@@ -191,3 +191,47 @@ def allclose_report(received: np.ndarray, expected: np.ndarray, rtol=1e-3, atol=
     if len(idx) > max_print:
         msgs.append(f"... and {len(idx) - max_print} more mismatched elements.")
     return msgs
+
+
+# ----------------------------------------------------------------------------- quantiser
+def quantize_ref(x: np.ndarray):
+    """fp32 (rows, K) -> (codes (rows, K/2) uint8, scales (rows, K/16) uint8 e4m3 bytes).
+
+    The input generation the benchmark configurations specify:
+    per 16-element block along K, scale = e4m3(amax / 6) rounded to nearest, ties to the even
+    code; each value becomes the nearest e2m1 code of x / scale (magnitude clamped to 6), ties
+    to the even code, -0 written as +0; element 2i in the low nibble.  Restated here by
+    exhaustive nearest-value search over the two code tables (the product's host version,
+    nvfp4_hackathon_b200.inputs.quantize_nvfp4, uses bucketize and torch's fp8 cast; the GPU
+    kernel uses the hardware cvt), so the three are independent.  Scales of 480 or more
+    (amax >= 2880) fall outside e4m3 and are not covered.
+    """
+    x = np.asarray(x, dtype=np.float32)
+    rows, kk = x.shape
+    blk = x.reshape(rows, kk // SF_VEC, SF_VEC)
+    amax = np.abs(blk).max(axis=-1).astype(np.float32)
+    target = (amax / np.float32(6.0)).astype(np.float32)
+    e4m3 = _e4m3_table().astype(np.float64)
+    pos = np.arange(0, 0x7F)                    # +0 .. 448, byte order = value order
+    vals = e4m3[pos]
+    d = np.abs(target[..., None].astype(np.float64) - vals)
+    best = d.min(axis=-1, keepdims=True)
+    cand = d == best
+    # ties: the even code (the larger of two tied neighbours is odd iff the smaller is even)
+    idx = np.where(cand & (pos % 2 == 0), pos, 10_000).min(axis=-1)
+    idx = np.where(idx == 10_000, np.argmax(cand, axis=-1), idx)
+    scale_b = pos[idx].astype(np.uint8)
+    s32 = vals[idx].astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        v = np.where(s32[..., None] > 0, blk / np.where(s32 > 0, s32, 1)[..., None], 0).astype(np.float32)
+    mag = np.minimum(np.abs(v), np.float32(6.0)).astype(np.float64)
+    table = _e2m1_table()[:8].astype(np.float64)   # magnitudes of codes 0..7
+    dd = np.abs(mag[..., None] - table)
+    bb = dd.min(axis=-1, keepdims=True)
+    c = dd == bb
+    code = np.where(c & (np.arange(8) % 2 == 0), np.arange(8), 99).min(axis=-1)
+    code = np.where(code == 99, np.argmax(c, axis=-1), code).astype(np.uint8)
+    code = code | (((v < 0) & (code > 0)).astype(np.uint8) << 3)
+    code = code.reshape(rows, kk)
+    packed = (code[:, 0::2] | (code[:, 1::2] << 4)).astype(np.uint8)
+    return packed, scale_b

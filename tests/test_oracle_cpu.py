@@ -113,3 +113,32 @@ def test_small_gemm_against_explicit_sum():
         for j in range(3):
             exp = sum(A[i, kk] * sa[i, kk // 16, 0] * B[j, kk] * sb[j, kk // 16, 0] for kk in range(64))
             assert c[0, i, j] == np.float16(exp)
+
+
+def test_quantiser_restatements_agree():
+    """The oracle's quantiser (exhaustive nearest-value search) and the host generator used for
+    the benchmark inputs (bucketize + torch's fp8 cast) give the same codes and scales, on
+    N(0, 1) data over a wide range of magnitudes and on values placed exactly on the e2m1
+    rounding midpoints of many scales (the ties)."""
+    import torch
+    from nvfp4_hackathon_b200.inputs import quantize_nvfp4
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((96, 512)).astype(np.float32)
+    x *= (2.0 ** rng.integers(-12, 8, size=(96, 1))).astype(np.float32)
+    # ties: blocks whose amax is 6 * s (scale exactly s) holding the midpoints * s
+    mids = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, -0.75, -2.5, 0.0, 6.0, -5.0,
+                     1.0, 3.0, 4.0, -6.0], dtype=np.float32)
+    scales = _e4m3_vals_for_test()
+    ties = np.stack([mids * s for s in scales]).astype(np.float32)  # each row: one block of 16
+    ties = ties.reshape(-1, 64) if ties.shape[0] % 4 == 0 else ties[: ties.shape[0] // 4 * 4].reshape(-1, 64)
+    for arr in (x, ties):
+        c_ref, s_ref = orc.quantize_ref(arr)
+        c_t, s_t = quantize_nvfp4(torch.from_numpy(arr))
+        assert np.array_equal(s_ref, s_t.view(torch.uint8).numpy())
+        assert np.array_equal(c_ref, c_t.numpy())
+
+
+def _e4m3_vals_for_test():
+    # positive normal e4m3 values from 2^-6 to 448 whose 6x stays finite in fp32
+    vals = [v for v in orc.E4M3[1:0x7F] if v >= 2.0 ** -6]
+    return np.array(vals, dtype=np.float32)

@@ -151,8 +151,8 @@ def custom_kernel(data: group_input_t, opt=None) -> group_output_t:
         sms = _SM_COUNT.get(device.index)
         if sms is None:
             sms = _SM_COUNT[device.index] = torch.cuda.get_device_properties(device).multi_processor_count
-        if opt is None:
-            opt = _native.options()
+        # (a copy: the caller's options are left as they were)
+        opt = _native.options() if opt is None else _native.Nvfp4Options.from_buffer_copy(opt)
         if opt.operand_order == 0 and opt.cta_pair == 0:
             opt.operand_order, opt.tile_n = choose_order(sizes, sms)
         elif opt.operand_order == 1 or opt.cta_pair == 2:

@@ -95,12 +95,30 @@ __device__ __forceinline__ float quotient_rn(float x, float s, float inv) {
   return __fmaf_rn(r, inv, q);
 }
 
+// The same three steps on two values at once with the packed fp32 instructions of sm_100
+// (mul/fma .rn.f32x2: each half rounds exactly like the scalar instruction, so the results
+// are bit for bit those of quotient_rn); ns = -s.
+__device__ __forceinline__ void quotient_rn2(float x0, float x1, float ns, float inv, float& v0,
+                                             float& v1) {
+  uint64_t X, NS, INV, Q, R, V;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(X) : "f"(x0), "f"(x1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(NS) : "f"(ns));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(INV) : "f"(inv));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(Q) : "l"(X), "l"(INV));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(R) : "l"(Q), "l"(NS), "l"(X));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(V) : "l"(R), "l"(INV), "l"(Q));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v0), "=f"(v1) : "l"(V));
+}
+
 __device__ __forceinline__ uint32_t e2m1_pack8(const float (&v)[8], float s, float inv) {
   uint32_t w = 0;
   if (s > 0.f) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      w |= cvt_e2m1x2(quotient_rn(v[2 * i], s, inv), quotient_rn(v[2 * i + 1], s, inv)) << (8 * i);
+    for (int i = 0; i < 4; ++i) {
+      float q0, q1;
+      quotient_rn2(v[2 * i], v[2 * i + 1], -s, inv, q0, q1);
+      w |= cvt_e2m1x2(q0, q1) << (8 * i);
+    }
   }
   const uint32_t zero = ~(w | (w >> 1) | (w >> 2)) & 0x11111111u;  // magnitude-0 nibbles
   return w & ~(zero << 3);
@@ -155,8 +173,32 @@ nvfp4_quantize_kernel(const void* __restrict__ x, int rows, int k, uint8_t* __re
       load8<DT>(&raw[b][0], *reinterpret_cast<float(*)[8]>(&v[0]));
       if constexpr (EPL == 16) load8<DT>(&raw[b][1], *reinterpret_cast<float(*)[8]>(&v[8]));
       float amax = 0.f;
+      if constexpr (DT == kQuantF32) {
 #pragma unroll
-      for (int i = 0; i < EPL; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        for (int i = 0; i < EPL; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      } else {
+        // |x| of two 16-bit values at once (clear both sign bits), then a max tree of packed
+        // maxima: exact, and like fmaxf a NaN operand yields the other one
+        const uint32_t w[8] = {raw[b][0].x, raw[b][0].y, raw[b][0].z, raw[b][0].w,
+                               raw[b][1].x, raw[b][1].y, raw[b][1].z, raw[b][1].w};
+        uint32_t m = w[0] & 0x7fff7fffu;
+#pragma unroll
+        for (int i = 1; i < 8; ++i) {
+          const uint32_t a = w[i] & 0x7fff7fffu;
+          if constexpr (DT == kQuantBF16) asm("max.bf16x2 %0, %0, %1;" : "+r"(m) : "r"(a));
+          else asm("max.f16x2 %0, %0, %1;" : "+r"(m) : "r"(a));
+        }
+        float lo, hi;
+        if constexpr (DT == kQuantBF16) {
+          lo = __uint_as_float(m << 16);
+          hi = __uint_as_float(m & 0xffff0000u);
+        } else {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&m));
+          lo = f.x;
+          hi = f.y;
+        }
+        amax = fmaxf(lo, hi);
+      }
       if constexpr (EPL == 8) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       if (row >= rows || !lane_ok) continue;
       // amax / 6 correctly rounded (1.0f / 6.0f folds to RN(1/6) at compile time; a

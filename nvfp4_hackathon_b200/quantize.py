@@ -59,6 +59,7 @@ def _main():
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--dtype", default="bf16", choices=["f32", "f16", "bf16"])
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--graph", action="store_true", help="time the calls replayed from a CUDA graph")
     args = ap.parse_args()
     dt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[args.dtype]
     # three inputs so consecutive calls do not find their input in L2
@@ -67,14 +68,26 @@ def _main():
         quantize(x, plain=False)
     torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    ev[0].record()
-    for i in range(args.reps):
-        quantize(xs[i % 3], plain=False)
-    ev[1].record()
+    if args.graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(args.reps):
+                quantize(xs[i % 3], plain=False)
+        g.replay()
+        torch.cuda.synchronize()
+        ev[0].record()
+        g.replay()
+        ev[1].record()
+    else:
+        ev[0].record()
+        for i in range(args.reps):
+            quantize(xs[i % 3], plain=False)
+        ev[1].record()
     torch.cuda.synchronize()
     us = ev[0].elapsed_time(ev[1]) * 1e3 / args.reps
     nbytes = args.rows * args.k * (xs[0].element_size() + 0.5 + 1.0 / 16)
-    print(json.dumps({"rows": args.rows, "k": args.k, "dtype": args.dtype, "us_per_call": round(us, 2),
+    print(json.dumps({"rows": args.rows, "k": args.k, "dtype": args.dtype, "graph": args.graph,
+                      "us_per_call": round(us, 2),
                       "gb_per_s": round(nbytes / us / 1e3, 1)}))
 
 
